@@ -1,0 +1,357 @@
+"""breccia's hot path on B200: ``cast``, ``dequantize``, ``requantize``,
+``matmul`` (and the K-major ``linear``) for CUDA torch tensors.
+
+Signatures, result conventions and error messages follow the reference
+(jvoltci/breccia v0.1.3):
+
+* ``cast(x, recipe)`` -- ``src/breccia/kernels/reference/cast.py:64-92``
+* ``dequantize(st)`` -- ``cast.py:95-118``
+* ``requantize(st, recipe)`` -- ``cast.py:339-346``
+* ``matmul(a, b, out_dtype)`` -- ``src/breccia/kernels/reference/matmul.py:42-133``
+
+Result conventions (``cast.py:170-217`` for per-tensor/block FP8, ``cast.py:124-161``
+for the others): per-tensor and block FP8 data are ``torch.float8_e4m3fn`` /
+``float8_e5m2``; MXFP8, NVFP4 and INT4 data are ``uint8`` with one code per
+byte; scales and zero points have the reference's dtypes and shapes; the
+result's ``recipe`` is the object passed in; everything stays on the input's
+device. Codes and scales equal the reference NumPy path's bit for bit (the
+reference's own torch path rounds FP8 ties to even through ATen and so
+differs from its NumPy path; this backend follows the NumPy path).
+
+Only CUDA tensors are accepted: there is no CPU fallback. ``install()``
+routes CUDA inputs of the real ``breccia`` package here and leaves every
+other input on breccia's own code.
+"""
+
+from __future__ import annotations
+
+import weakref
+from typing import Any, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import types as T
+
+__all__ = ["cast", "dequantize", "requantize", "matmul", "linear", "gemm_operands"]
+
+_TORCH_FP8 = {"E4M3": torch.float8_e4m3fn, "E5M2": torch.float8_e5m2}
+_FMT = {"E4M3": _lib.FP8_E4M3, "E5M2": _lib.FP8_E5M2}
+_IN_DT = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+          torch.float16: _lib.DTYPE_F16}
+_OUT_DT = _IN_DT
+
+
+# ----------------------------------------------------------------- plumbing
+
+
+def _classes(recipe):
+    """ScaledTensor and layout classes of the recipe's own package, so that a
+    recipe from the real breccia gets a breccia.ScaledTensor back."""
+    mod = type(recipe).__module__
+    if mod == "breccia" or mod.startswith("breccia."):
+        import breccia
+        return breccia.ScaledTensor, breccia
+    return T.ScaledTensor, T
+
+
+def _stream(dev) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(x, what="x"):
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise TypeError(
+            f"breccia_b200 operates on CUDA torch tensors; {what} is "
+            f"{type(x).__name__}{'' if not isinstance(x, torch.Tensor) else ' on ' + str(x.device)}")
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _input(x) -> torch.Tensor:
+    _require_cuda(x)
+    if x.dtype not in _IN_DT:
+        x = x.to(torch.float32)  # np.asarray(x, dtype=np.float32), cast.py:77
+    return _aligned(x)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+# Side data the tensor-core GEMMs consume (scales in the tcgen05 layout,
+# packed FP4/INT4 nibbles), keyed by the identity of a ScaledTensor's data
+# tensor and dropped when that tensor is freed.
+_SIDE: dict = {}
+
+
+def _remember(data: torch.Tensor, **side) -> None:
+    key = id(data)
+    if key not in _SIDE:
+        weakref.finalize(data, _SIDE.pop, key, None)
+    _SIDE.setdefault(key, {}).update(side)
+
+
+def _side(data: torch.Tensor) -> dict:
+    return _SIDE.get(id(data), {})
+
+
+def _mma_scale_shape(rows: int, scale_cols: int):
+    return (((rows + 127) // 128) * ((scale_cols + 3) // 4) * 512,)
+
+
+# ------------------------------------------------------------------- cast
+
+
+def cast(x: Any, recipe: Any, *, block_m: Optional[int] = None):
+    """Quantize a CUDA tensor with ``recipe`` (``cast.py:64-92``).
+
+    ``block_m`` (extension, ``Float8BlockScaling`` only): scale
+    ``block_m x block_k`` tiles of the last two axes instead of ``1 x block_k``
+    runs -- the DeepSeek-v3 128x128 weight layout, ``PerBlockMN(block_m,
+    block_k)``. The reference can describe but not produce it.
+    """
+    x = _input(x)
+    ST, L = _classes(recipe)
+    name = getattr(recipe, "name", None)
+    dev = x.device
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        if name in ("delayed", "current"):
+            return _cast_per_tensor(x, recipe, ST, L, st)
+        if name == "block":
+            return _cast_block(x, recipe, ST, L, st, block_m)
+        if name == "mxfp8":
+            return _cast_mxfp8(x, recipe, ST, L, st)
+        if name == "nvfp4":
+            return _cast_nvfp4(x, recipe, ST, L, st)
+        if name == "int4":
+            return _cast_int4(x, recipe, ST, L, st)
+    raise TypeError(f"unsupported recipe: {type(recipe).__name__}")
+
+
+def _cast_per_tensor(x, recipe, ST, L, st):
+    fmt = recipe.fp8_format
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    ws = torch.empty(1, dtype=torch.int32, device=x.device)
+    _lib.call("brc_cast_pertensor_fp8", x.data_ptr(), _IN_DT[x.dtype], x.numel(), _FMT[fmt],
+              codes.data_ptr(), scale.data_ptr(), ws.data_ptr(), st)
+    return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe, layout=L.PerTensor())
+
+
+def _last_axis_checks(x, recipe_cls_name, block, msg_kind):
+    if x.ndim < 2:
+        raise ValueError(f"{recipe_cls_name} requires x.ndim >= 2, got {x.ndim}")
+    K = x.shape[-1]
+    if K % block != 0:
+        if msg_kind == "block_k":  # cast.py:203-204
+            raise ValueError(f"K={K} must be divisible by block_k={block}")
+        if msg_kind == "group_size":  # cast.py:521-522
+            raise ValueError(f"K={K} must be divisible by group_size={block}")
+        # _utils.py:25-28 (block_amax)
+        raise ValueError(f"last-axis size {K} must be divisible by block_size {block}")
+    return K
+
+
+def _cast_block(x, recipe, ST, L, st, block_m):
+    B = recipe.block_k
+    fmt = recipe.fp8_format
+    K = _last_axis_checks(x, "Float8BlockScaling", B, "block_k")
+    rows = x.numel() // K if K else 0
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    if block_m is None:
+        scale = torch.empty(x.shape[:-1] + (K // B,), dtype=torch.float32, device=x.device)
+        _lib.call("brc_cast_block_fp8", x.data_ptr(), _IN_DT[x.dtype], rows, K, B, _FMT[fmt],
+                  codes.data_ptr(), scale.data_ptr(), st)
+        layout = L.PerBlockK(block_size=B)
+    else:
+        M = x.shape[-2]
+        if M % block_m:
+            raise ValueError(f"M={M} must be divisible by block_m={block_m}")
+        scale = torch.empty(x.shape[:-2] + (M // block_m, K // B), dtype=torch.float32,
+                            device=x.device)
+        _lib.call("brc_cast_block_fp8_2d", x.data_ptr(), _IN_DT[x.dtype], rows, K, block_m, B,
+                  _FMT[fmt], codes.data_ptr(), scale.data_ptr(), st)
+        layout = L.PerBlockMN(block_m=block_m, block_n=B)
+    return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe, layout=layout)
+
+
+def _cast_mxfp8(x, recipe, ST, L, st):
+    fmt = recipe.fp8_format
+    K = _last_axis_checks(x, "MXFP8BlockScaling", 32, "block_size")
+    rows = x.numel() // K if K else 0
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scale = torch.empty(x.shape[:-1] + (K // 32,), dtype=torch.uint8, device=x.device)
+    sf_mma = torch.zeros(_mma_scale_shape(rows, K // 32), dtype=torch.uint8, device=x.device)
+    _lib.call("brc_cast_mxfp8", x.data_ptr(), _IN_DT[x.dtype], rows, K, _FMT[fmt],
+              codes.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
+    _remember(codes, sf_mma=sf_mma)
+    return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockMN(block_m=1, block_n=32))
+
+
+def _cast_nvfp4(x, recipe, ST, L, st):
+    K = _last_axis_checks(x, "NVFP4BlockScaling", 16, "block_size")
+    rows = x.numel() // K if K else 0
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    packed = torch.empty(x.shape[:-1] + (K // 2,), dtype=torch.uint8, device=x.device)
+    scale = torch.empty(x.shape[:-1] + (K // 16,), dtype=torch.uint8, device=x.device)
+    sf_mma = torch.zeros(_mma_scale_shape(rows, K // 16), dtype=torch.uint8, device=x.device)
+    _lib.call("brc_cast_nvfp4", x.data_ptr(), _IN_DT[x.dtype], rows, K, codes.data_ptr(),
+              packed.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
+    _remember(codes, packed=packed, sf_mma=sf_mma)
+    return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockMN(block_m=1, block_n=16))
+
+
+def _cast_int4(x, recipe, ST, L, st):
+    G = recipe.group_size
+    K = _last_axis_checks(x, "INT4Scaling", G, "group_size")
+    rows = x.numel() // K if K else 0
+    sdt = torch.float16 if recipe.scale_dtype == "fp16" else torch.float32  # cast.py:512-513
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    packed = torch.empty(x.shape[:-1] + (K // 2,), dtype=torch.uint8, device=x.device) \
+        if G % 2 == 0 else None
+    scale = torch.empty(x.shape[:-1] + (K // G,), dtype=sdt, device=x.device)
+    zp = None if recipe.symmetric else torch.empty_like(scale)
+    _lib.call("brc_cast_int4", x.data_ptr(), _IN_DT[x.dtype], rows, K, G,
+              int(bool(recipe.signed)), int(bool(recipe.symmetric)),
+              _lib.SCALE_F16 if sdt == torch.float16 else _lib.SCALE_F32,
+              codes.data_ptr(), _ptr(packed), scale.data_ptr(), _ptr(zp), st)
+    if packed is not None:
+        _remember(codes, packed=packed)
+    return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockK(block_size=G),
+              zero_point=zp)
+
+
+# ------------------------------------------------------------- dequantize
+
+
+def _codes_u8(data: torch.Tensor) -> torch.Tensor:
+    _require_cuda(data, "ScaledTensor.data")
+    if data.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+        data = data.view(torch.uint8)
+    if data.dtype != torch.uint8:
+        raise TypeError(f"unsupported data dtype {data.dtype}")
+    return _aligned(data)
+
+
+def dequantize(scaled, out_dtype=torch.float32):
+    """``decode(data) * scale`` as float32 (``cast.py:95-118``).
+
+    ``out_dtype`` (extension): ``torch.bfloat16`` / ``torch.float16`` write
+    the same products rounded to that type.
+    """
+    r = scaled.recipe
+    name = getattr(r, "name", None)
+    codes = _codes_u8(scaled.data)
+    dev = codes.device
+    if out_dtype not in _OUT_DT:
+        raise TypeError(f"out_dtype must be float32, bfloat16 or float16, got {out_dtype}")
+    out = torch.empty(codes.shape, dtype=out_dtype, device=dev)
+    odt = _OUT_DT[out_dtype]
+    scale = _aligned(scaled.scale)
+    K = codes.shape[-1] if codes.ndim else 1
+    rows = codes.numel() // K if K else 0
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        if name in ("delayed", "current"):
+            _lib.call("brc_dequant_pertensor_fp8", codes.data_ptr(), codes.numel(),
+                      _FMT[r.fp8_format], scale.to(torch.float32).data_ptr(), out.data_ptr(),
+                      odt, st)
+        elif name == "block":
+            lay = scaled.layout
+            bm = getattr(lay, "block_m", 1) if getattr(lay, "name", "") == "per_block_mn" else 1
+            _lib.call("brc_dequant_block_fp8", codes.data_ptr(), rows, K, bm, r.block_k,
+                      _FMT[r.fp8_format], scale.data_ptr(), out.data_ptr(), odt, st)
+        elif name == "mxfp8":
+            _lib.call("brc_dequant_mxfp8", codes.data_ptr(), rows, K, _FMT[r.fp8_format],
+                      scale.data_ptr(), out.data_ptr(), odt, st)
+        elif name == "nvfp4":
+            _lib.call("brc_dequant_nvfp4", codes.data_ptr(), rows, K, scale.data_ptr(),
+                      out.data_ptr(), odt, st)
+        elif name == "int4":
+            zp = scaled.zero_point
+            sdt = _lib.SCALE_F16 if scale.dtype == torch.float16 else _lib.SCALE_F32
+            if zp is not None:
+                zp = _aligned(zp.to(scale.dtype))
+            _lib.call("brc_dequant_int4", codes.data_ptr(), rows, K, r.group_size,
+                      int(bool(r.signed)), sdt, scale.data_ptr(), _ptr(zp), out.data_ptr(),
+                      odt, st)
+        else:
+            raise TypeError(f"unsupported recipe: {type(r).__name__}")
+    return out
+
+
+# -------------------------------------------------------------- requantize
+
+
+def requantize(scaled, recipe):
+    """``cast(dequantize(st), recipe)`` (``cast.py:339-346``). NVFP4 -> MXFP8
+    runs as one fused kernel; other pairs dequantize to float32 first."""
+    src = getattr(scaled.recipe, "name", None)
+    if src == "nvfp4" and getattr(recipe, "name", None) == "mxfp8":
+        codes = _codes_u8(scaled.data)
+        K = codes.shape[-1]
+        if codes.ndim < 2 or K % 32:
+            return cast(dequantize(scaled), recipe)
+        rows = codes.numel() // K
+        ST, L = _classes(recipe)
+        dev = codes.device
+        out = torch.empty(codes.shape, dtype=torch.uint8, device=dev)
+        scale = torch.empty(codes.shape[:-1] + (K // 32,), dtype=torch.uint8, device=dev)
+        sf_mma = torch.zeros(_mma_scale_shape(rows, K // 32), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("brc_requant_nvfp4_to_mxfp8", codes.data_ptr(),
+                      _aligned(scaled.scale).data_ptr(), rows, K, _FMT[recipe.fp8_format],
+                      out.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), _stream(dev))
+        _remember(out, sf_mma=sf_mma)
+        return ST(data=out, scale=scale, recipe=recipe,
+                  layout=L.PerBlockMN(block_m=1, block_n=32))
+    return cast(dequantize(scaled), recipe)
+
+
+# ------------------------------------------------------------------ matmul
+
+
+def _torch_out_dtype(out_dtype):
+    """``matmul.py:136-147``, extended to accept torch dtypes (incl. bfloat16)."""
+    if isinstance(out_dtype, torch.dtype):
+        return out_dtype
+    key = np.dtype(out_dtype).type
+    return {np.float32: torch.float32, np.float64: torch.float64,
+            np.float16: torch.float16}.get(key, torch.float32)
+
+
+def _is_scaled(t) -> bool:
+    return hasattr(t, "recipe") and hasattr(t, "scale") and hasattr(t, "data")
+
+
+def matmul(a, b, out_dtype=np.float32):
+    """Scaled matmul with the reference's semantics (``matmul.py:42-133``):
+    ``a (..., M, K) @ b (..., K, N)`` of the dequantized operands with
+    float32 accumulation, then ``out_dtype`` (a NumPy dtype as in the
+    reference, or a torch dtype such as ``torch.bfloat16``)."""
+    from . import gemm
+    return gemm.matmul(a, b, _torch_out_dtype(out_dtype))
+
+
+def linear(a, w, out_dtype=torch.bfloat16):
+    """``a @ w.T`` with ``w`` an ``(N, K)`` ScaledTensor whose blocks run
+    along K (a weight cast in nn.Linear orientation). This is the layout the
+    block-scaled tensor-core GEMMs consume directly."""
+    from . import gemm
+    return gemm.linear(a, w, _torch_out_dtype(out_dtype))
+
+
+def gemm_operands(scaled) -> dict:
+    """Tensor-core side data recorded by ``cast`` for ``scaled``: ``sf_mma``
+    (scales in the tcgen05 layout) and/or ``packed`` (two 4-bit codes per byte,
+    element 2i in the low nibble)."""
+    return dict(_side(scaled.data if scaled.data.dtype == torch.uint8
+                      else scaled.data))

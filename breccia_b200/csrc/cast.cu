@@ -1,0 +1,1114 @@
+// Cast / dequantize / requantize kernels for every breccia recipe (sm_100a).
+//
+// All row-local recipes (Float8BlockScaling 1 x block_k, MXFP8, NVFP4, INT4)
+// share one kernel shape. Because blocks run along the last axis and the
+// row length is a multiple of the block, a row-major (rows, cols) tensor is
+// a flat sequence of contiguous blocks, and the row-major scale tensor is
+// indexed by the flat block number. Each warp processes "tiles" of
+// 32 / LPB blocks; LPB adjacent lanes share one block, each lane owning
+// B / LPB contiguous elements loaded as 16-byte vectors. The block statistic
+// (abs-max, or min and max) is reduced with xor-shuffles over those lanes.
+// Grids are sized to the SM count and loop over tiles.
+//
+// HBM traffic per element is the input read plus the code write; the kernels
+// keep the per-element instruction count low enough (~10-14 ops) that a
+// 2-byte input stays bandwidth-bound.
+
+#include "common.cuh"
+#include "e8m0_thresholds.h"
+#include "launch.h"
+
+namespace brc {
+
+__device__ const uint32_t g_e8m0_thr[kE8m0Binades] = {BRC_E8M0_THRESHOLDS};
+
+// n / d for n < 2^32 with a precomputed 33-bit multiplier (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994).
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+static FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  FastDiv f;
+  f.d = d;
+  f.shift = l;
+  f.mul = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+  return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)__umulhi(n, f.mul) + n) >> f.shift);
+}
+
+// Byte offset of scale (row, col) in the tcgen05 block-scale layout.
+__device__ __forceinline__ uint32_t sf_mma_offset(uint32_t row, uint32_t col,
+                                                  uint32_t col_tiles) {
+  return ((row >> 7) * col_tiles + (col >> 2)) * 512u + (row & 31u) * 16u +
+         ((row >> 5) & 3u) * 4u + (col & 3u);
+}
+
+// --------------------------------------------------------------- helpers
+template <int NW>
+__device__ __forceinline__ void store_words(uint8_t* p, const uint32_t* w) {
+  if constexpr (NW == 1) {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  } else if constexpr (NW == 2) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW; i += 4)
+      stg16(p + 4 * i, make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]));
+  }
+}
+
+// Pack unpacked FP4/INT4 code words (one code per byte, 4 per word) two per
+// byte, element 2i in the low nibble.
+template <int NW>
+__device__ __forceinline__ void store_packed(uint8_t* p, const uint32_t* w) {
+  uint32_t out[NW / 2];
+#pragma unroll
+  for (int i = 0; i < NW / 2; ++i) {
+    const uint32_t a = w[2 * i] | (w[2 * i] >> 4);
+    const uint32_t b = w[2 * i + 1] | (w[2 * i + 1] >> 4);
+    out[i] = prmt(a, b, 0x6420);
+  }
+  store_words<NW / 2>(p, out);
+}
+
+template <int DT>
+__device__ __forceinline__ void vec_minmax(const uint4 v, float& mn, float& mx) {
+  float f[In<DT>::kVec];
+  unpack<DT>(v, f);
+#pragma unroll
+  for (int i = 0; i < In<DT>::kVec; ++i) {
+    mn = fmin_nan(mn, f[i]);
+    mx = fmax_nan(mx, f[i]);
+  }
+}
+
+template <int DT>
+constexpr int elem_bytes() { return DT == BRC_DTYPE_F32 ? 4 : 2; }
+
+// Power of two 2^k as a float32 for k in [-149, 127] (exact).
+__device__ __forceinline__ float exp2i(int k) {
+  if (k >= -126) return __uint_as_float((uint32_t)(k + 127) << 23);
+  return __uint_as_float(1u << (k + 149));
+}
+
+// --------------------------------------------------------------- modes
+enum Mode { kBlockFp8 = 0, kMxfp8 = 1, kNvfp4 = 2, kInt4Sym = 3, kInt4Asym = 4 };
+
+struct BlockCastArgs {
+  const void* x;
+  uint8_t* codes;       // one code per element, or null (nvfp4/int4)
+  uint8_t* packed;      // two per byte, or null
+  void* scales;
+  void* zp;
+  uint8_t* scales_mma;  // tcgen05 layout, or null
+  int64_t n_blocks;
+  FastDiv blocks_per_row;
+  uint32_t sf_col_tiles;
+  int is_signed;
+  int scale_f16;
+};
+
+template <int E>
+struct LaneVals {
+  float f[E];
+};
+
+// Encode one lane's E values given the block's scale; writes codes/packed.
+template <int MODE, int FMT, int E>
+__device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, const float* f,
+                                            float s, float zp, bool fast) {
+  constexpr int NW = E / 4;
+  uint32_t w[NW];
+  if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
+    if (fast) {
+      if constexpr (MODE == kMxfp8) {
+        // s holds the exact power-of-two reciprocal of the E8M0 scale.
+#pragma unroll
+        for (int j = 0; j < NW; ++j)
+          w[j] = enc4_fp8<FMT>(__fmul_rn(f[4 * j], s), __fmul_rn(f[4 * j + 1], s),
+                               __fmul_rn(f[4 * j + 2], s), __fmul_rn(f[4 * j + 3], s));
+      } else {
+        const float r = __frcp_rn(s);
+#pragma unroll
+        for (int j = 0; j < NW; ++j)
+          w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
+                               div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NW; ++j) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * j + i], s)) << (8 * i);
+        w[j] = c;
+      }
+    }
+    store_words<NW>(a.codes + e0, w);
+  } else if constexpr (MODE == kNvfp4) {
+    if (fast) {
+      const float r = __frcp_rn(s);
+#pragma unroll
+      for (int j = 0; j < NW; ++j)
+        w[j] = enc4_e2m1(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
+                         div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+    } else {
+#pragma unroll
+      for (int j = 0; j < NW; ++j) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c |= enc1_e2m1(div_ieee(f[4 * j + i], s)) << (8 * i);
+        w[j] = c;
+      }
+    }
+    if (a.codes) store_words<NW>(a.codes + e0, w);
+    if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
+  } else {
+    // INT4: np.round(np.clip(v, lo, hi)) with half-to-even rounding via the
+    // 1.5 * 2^23 addition; the low nibble of the sum's bits is the code.
+    const float lo = (MODE == kInt4Sym && a.is_signed) ? -8.f : 0.f;
+    const float hi = (MODE == kInt4Sym && a.is_signed) ? 7.f : 15.f;
+    const float r = fast ? __frcp_rn(s) : 0.f;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+      uint32_t c = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float q = fast ? div_by(f[4 * j + i], s, r) : div_ieee(f[4 * j + i], s);
+        if constexpr (MODE == kInt4Asym) q = __fadd_rn(q, zp);
+        uint32_t code;
+        if (!fast && isnan(q)) {
+          code = 0u;  // NumPy's float->uint8 conversion of NaN gives 0
+        } else {
+          const float v = fminf(fmaxf(q, lo), hi);
+          code = __float_as_uint(__fadd_rn(v, 12582912.f)) & 0xFu;
+        }
+        c |= code << (8 * i);
+      }
+      w[j] = c;
+    }
+    if (a.codes) store_words<NW>(a.codes + e0, w);
+    if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
+  }
+}
+
+template <int DT, int MODE, int FMT, int B, int LPB>
+__global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
+  constexpr int V = In<DT>::kVec;
+  constexpr int E = B / LPB;
+  constexpr int NV = E / V;
+  constexpr int BPW = 32 / LPB;
+  static_assert(E % V == 0 && E % 8 == 0, "lane chunk must be whole vectors");
+  const int lane = threadIdx.x & 31;
+  const int part = lane % LPB;
+  const int64_t n_warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t n_tiles = (a.n_blocks + BPW - 1) / BPW;
+  for (int64_t tile = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       tile < n_tiles; tile += n_warps) {
+    const int64_t blk = tile * BPW + lane / LPB;
+    const bool valid = blk < a.n_blocks;
+    const int64_t e0 = blk * B + (int64_t)part * E;
+    uint4 v[NV];
+    float st0, st1;  // abs-max, or (min, max) for asymmetric INT4
+    if constexpr (MODE == kInt4Asym) {
+      st0 = __int_as_float(0x7F800000);
+      st1 = -__int_as_float(0x7F800000);
+    } else {
+      st0 = 0.f;
+      st1 = 0.f;
+    }
+    if (valid) {
+      const char* src = static_cast<const char*>(a.x) + e0 * elem_bytes<DT>();
+#pragma unroll
+      for (int i = 0; i < NV; ++i) v[i] = ldg16(src + 16 * i);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if constexpr (MODE == kInt4Asym) vec_minmax<DT>(v[i], st0, st1);
+        else st0 = fmax_nan(st0, vec_absmax<DT>(v[i]));
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < LPB; o <<= 1) {
+      if constexpr (MODE == kInt4Asym) {
+        st0 = fmin_nan(st0, __shfl_xor_sync(0xFFFFFFFFu, st0, o));
+        st1 = fmax_nan(st1, __shfl_xor_sync(0xFFFFFFFFu, st1, o));
+      } else {
+        st0 = fmax_nan(st0, __shfl_xor_sync(0xFFFFFFFFu, st0, o));
+      }
+    }
+    if (!valid) continue;
+
+    float f[E];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) unpack<DT>(v[i], f + i * V);
+
+    float s, zp = 0.f;
+    bool fast;
+    if constexpr (MODE == kBlockFp8) {
+      constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+      s = __fdiv_rn(fmax_nan(st0, 1e-10f), kMax);
+      if (part == 0) static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      fast = isfinite(s);
+    } else if constexpr (MODE == kMxfp8) {
+      constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+      const float am = fmax_nan(st0, 1e-10f);
+      const uint32_t e = e8m0_code(__fdiv_rn(am, kMax), g_e8m0_thr);
+      if (part == 0) {
+        static_cast<uint8_t*>(a.scales)[blk] = (uint8_t)e;
+        if (a.scales_mma) {
+          const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
+          const uint32_t col = (uint32_t)blk - row * a.blocks_per_row.d;
+          a.scales_mma[sf_mma_offset(row, col, a.sf_col_tiles)] = (uint8_t)e;
+        }
+      }
+      fast = isfinite(am);
+      // fast: multiply by 2^(127-e) (exact); slow: IEEE divide by 2^(e-127).
+      s = fast ? exp2i(127 - (int)e)
+               : (e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127));
+    } else if constexpr (MODE == kNvfp4) {
+      const float am = fmax_nan(st0, 1e-10f);
+      const uint32_t sc = enc1_e4m3(__fdiv_rn(am, 6.f));
+      float actual = dec_e4m3(sc);
+      if (!(actual > 0.f)) actual = 0x1p-9f;  // np.where(actual > 0, actual, 2^-9)
+      if (part == 0) {
+        static_cast<uint8_t*>(a.scales)[blk] = (uint8_t)sc;
+        if (a.scales_mma) {
+          const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
+          const uint32_t col = (uint32_t)blk - row * a.blocks_per_row.d;
+          a.scales_mma[sf_mma_offset(row, col, a.sf_col_tiles)] = (uint8_t)sc;
+        }
+      }
+      s = actual;
+      fast = isfinite(am);
+    } else if constexpr (MODE == kInt4Sym) {
+      s = __fdiv_rn(fmax_nan(st0, 1e-10f), a.is_signed ? 7.f : 15.f);
+      if (part == 0) {
+        if (a.scale_f16) static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
+        else static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      }
+      fast = isfinite(s);
+    } else {
+      const float range = fmax_nan(__fsub_rn(st1, st0), 1e-10f);
+      s = __fdiv_rn(range, 15.f);
+      const float zf = rintf(__fdiv_rn(-st0, s));
+      // np.clip keeps the operand (including -0.0 and NaN) when it is in range
+      zp = zf < 0.f ? 0.f : (zf > 15.f ? 15.f : zf);
+      if (part == 0) {
+        if (a.scale_f16) {
+          static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
+          static_cast<__half*>(a.zp)[blk] = to_half_canon(zp);
+        } else {
+          static_cast<float*>(a.scales)[blk] = canon_nan(s);
+          static_cast<float*>(a.zp)[blk] = canon_nan(zp);
+        }
+      }
+      fast = isfinite(s) && isfinite(zp);
+    }
+    encode_lane<MODE, FMT, E>(a, e0, f, s, zp, fast);
+  }
+}
+
+// Generic fallback: one thread per block, any block size, scalar loads.
+template <int DT>
+__device__ __forceinline__ float load1(const void* x, int64_t i) {
+  if constexpr (DT == BRC_DTYPE_F32) return static_cast<const float*>(x)[i];
+  else if constexpr (DT == BRC_DTYPE_BF16)
+    return __uint_as_float((uint32_t)static_cast<const uint16_t*>(x)[i] << 16);
+  else return __half2float(static_cast<const __half*>(x)[i]);
+}
+
+template <int DT, int MODE, int FMT>
+__global__ void __launch_bounds__(256) k_block_cast_generic(BlockCastArgs a, int B) {
+  for (int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; blk < a.n_blocks;
+       blk += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = blk * B;
+    float amax = 0.f, mn = __int_as_float(0x7F800000), mx = -__int_as_float(0x7F800000);
+    for (int i = 0; i < B; ++i) {
+      const float v = load1<DT>(a.x, e0 + i);
+      amax = fmax_nan(amax, fabsf(v));
+      mn = fmin_nan(mn, v);
+      mx = fmax_nan(mx, v);
+    }
+    float s, zp = 0.f;
+    if constexpr (MODE == kBlockFp8) {
+      constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+      s = __fdiv_rn(fmax_nan(amax, 1e-10f), kMax);
+      static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      for (int i = 0; i < B; ++i)
+        a.codes[e0 + i] = (uint8_t)enc1_fp8<FMT>(div_ieee(load1<DT>(a.x, e0 + i), s));
+    } else if constexpr (MODE == kInt4Sym || MODE == kInt4Asym) {
+      if constexpr (MODE == kInt4Sym) {
+        s = __fdiv_rn(fmax_nan(amax, 1e-10f), a.is_signed ? 7.f : 15.f);
+      } else {
+        s = __fdiv_rn(fmax_nan(__fsub_rn(mx, mn), 1e-10f), 15.f);
+        const float zf = rintf(__fdiv_rn(-mn, s));
+        zp = zf < 0.f ? 0.f : (zf > 15.f ? 15.f : zf);
+      }
+      if (a.scale_f16) static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
+      else static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      if constexpr (MODE == kInt4Asym) {
+        if (a.scale_f16) static_cast<__half*>(a.zp)[blk] = to_half_canon(zp);
+        else static_cast<float*>(a.zp)[blk] = canon_nan(zp);
+      }
+      const float lo = (MODE == kInt4Sym && a.is_signed) ? -8.f : 0.f;
+      const float hi = (MODE == kInt4Sym && a.is_signed) ? 7.f : 15.f;
+      for (int i = 0; i < B; ++i) {
+        float q = div_ieee(load1<DT>(a.x, e0 + i), s);
+        if constexpr (MODE == kInt4Asym) q = __fadd_rn(q, zp);
+        const uint32_t code =
+            isnan(q) ? 0u : (__float_as_uint(__fadd_rn(fminf(fmaxf(q, lo), hi), 12582912.f)) & 0xFu);
+        if (a.codes) a.codes[e0 + i] = (uint8_t)code;
+        if (a.packed) {
+          // only reached with even B: element pairs never straddle blocks
+          uint8_t* p = a.packed + (e0 + i) / 2;
+          if (((e0 + i) & 1) == 0) *p = (uint8_t)code;
+          else *p = (uint8_t)(*p | (code << 4));
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------- per-tensor
+template <int DT>
+__global__ void __launch_bounds__(256) k_amax(const void* __restrict__ x, int64_t n,
+                                              uint32_t* amax_bits) {
+  constexpr int V = In<DT>::kVec;
+  const int64_t nvec = n / V;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float m = 0.f;
+  const char* base = static_cast<const char*>(x);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    const uint4 v0 = ldg16(base + 16 * i);
+    const uint4 v1 = ldg16(base + 16 * (i + stride));
+    const uint4 v2 = ldg16(base + 16 * (i + 2 * stride));
+    const uint4 v3 = ldg16(base + 16 * (i + 3 * stride));
+    m = fmax_nan(m, fmax_nan(fmax_nan(vec_absmax<DT>(v0), vec_absmax<DT>(v1)),
+                             fmax_nan(vec_absmax<DT>(v2), vec_absmax<DT>(v3))));
+  }
+  for (; i < nvec; i += stride) m = fmax_nan(m, vec_absmax<DT>(ldg16(base + 16 * i)));
+  for (int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
+    m = fmax_nan(m, fabsf(load1<DT>(x, t)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (threadIdx.x == 0 && __float_as_uint(m) != 0u) atomicMax(amax_bits, __float_as_uint(m));
+  }
+}
+
+__global__ void k_amax_reset(uint32_t* amax_bits) { *amax_bits = 0u; }
+
+// scale = float32(max(float64(amax), 1e-10) / fmt_max), as
+// src/breccia/kernels/reference/cast.py:368-370 computes it in float64.
+// For amax >= 1e-10 this equals float32 division (double rounding through
+// float64 is innocuous for division); below the floor it is the constant
+// float32(1e-10 / fmt_max) computed on the host.
+__device__ __forceinline__ float pertensor_scale(uint32_t bits, float fmt_max, float floor_scale) {
+  const float amax = __uint_as_float(bits);
+  if (isnan(amax)) return amax;
+  if ((double)amax < 1e-10) return floor_scale;
+  return __fdiv_rn(amax, fmt_max);
+}
+
+template <int DT, int FMT>
+__global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict__ x, int64_t n,
+                                                         const uint32_t* amax_bits,
+                                                         float floor_scale, uint8_t* codes,
+                                                         float* scale_out) {
+  constexpr int V = In<DT>::kVec;
+  constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+  const float s = pertensor_scale(*amax_bits, kMax, floor_scale);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = canon_nan(s);
+  const bool fast = isfinite(s);
+  const float r = __frcp_rn(s);
+  const int64_t nvec = n / V;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const char* base = static_cast<const char*>(x);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (fast) {
+    for (; i + stride < nvec; i += 2 * stride) {
+      const uint4 v0 = ldg16(base + 16 * i);
+      const uint4 v1 = ldg16(base + 16 * (i + stride));
+      float f0[V], f1[V];
+      unpack<DT>(v0, f0);
+      unpack<DT>(v1, f1);
+      uint32_t w0[V / 4], w1[V / 4];
+#pragma unroll
+      for (int j = 0; j < V / 4; ++j) {
+        w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
+                              div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
+        w1[j] = enc4_fp8<FMT>(div_by(f1[4 * j], s, r), div_by(f1[4 * j + 1], s, r),
+                              div_by(f1[4 * j + 2], s, r), div_by(f1[4 * j + 3], s, r));
+      }
+      store_words<V / 4>(codes + i * V, w0);
+      store_words<V / 4>(codes + (i + stride) * V, w1);
+    }
+    for (; i < nvec; i += stride) {
+      float f0[V];
+      unpack<DT>(ldg16(base + 16 * i), f0);
+      uint32_t w0[V / 4];
+#pragma unroll
+      for (int j = 0; j < V / 4; ++j)
+        w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
+                              div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
+      store_words<V / 4>(codes + i * V, w0);
+    }
+  } else {
+    for (; i < nvec; i += stride) {
+      float f0[V];
+      unpack<DT>(ldg16(base + 16 * i), f0);
+#pragma unroll
+      for (int j = 0; j < V; ++j) codes[i * V + j] = (uint8_t)enc1_fp8<FMT>(div_ieee(f0[j], s));
+    }
+  }
+  for (int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
+    codes[t] = (uint8_t)enc1_fp8<FMT>(div_ieee(load1<DT>(x, t), s));
+}
+
+// --------------------------------------------------------------- 2-D tiles
+// One CTA per (block_m x block_k) tile; the tile's vectors stay in registers
+// between the amax pass and the encode pass.
+template <int DT, int FMT, int MAXV>
+__global__ void __launch_bounds__(256) k_block2d_cast(const void* __restrict__ x, int64_t cols,
+                                                      int bm, int bk, uint8_t* codes,
+                                                      float* scales) {
+  constexpr int V = In<DT>::kVec;
+  constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+  const int vec_per_row = bk / V;
+  const int nvec = bm * vec_per_row;
+  const int64_t r0 = (int64_t)blockIdx.y * bm, c0 = (int64_t)blockIdx.x * bk;
+  uint4 v[MAXV];
+  float m = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int idx = threadIdx.x + k * blockDim.x;
+    if (idx < nvec) {
+      const int rr = idx / vec_per_row, cc = (idx % vec_per_row) * V;
+      v[k] = ldg16(static_cast<const char*>(x) + ((r0 + rr) * cols + c0 + cc) * elem_bytes<DT>());
+      m = fmax_nan(m, vec_absmax<DT>(v[k]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  __shared__ float red[8];
+  __shared__ float s_sh;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = fmax_nan(t, red[w]);
+    const float s = __fdiv_rn(fmax_nan(t, 1e-10f), kMax);
+    s_sh = s;
+    scales[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = canon_nan(s);
+  }
+  __syncthreads();
+  const float s = s_sh;
+  const bool fast = isfinite(s);
+  const float r = __frcp_rn(s);
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int idx = threadIdx.x + k * blockDim.x;
+    if (idx < nvec) {
+      const int rr = idx / vec_per_row, cc = (idx % vec_per_row) * V;
+      float f[V];
+      unpack<DT>(v[k], f);
+      uint32_t w[V / 4];
+#pragma unroll
+      for (int j = 0; j < V / 4; ++j) {
+        if (fast) {
+          w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
+                               div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+        } else {
+          uint32_t c = 0;
+          for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * j + i], s)) << (8 * i);
+          w[j] = c;
+        }
+      }
+      store_words<V / 4>(codes + (r0 + rr) * cols + c0 + cc, w);
+    }
+  }
+}
+
+// --------------------------------------------------------------- dequantize
+// 16 codes per lane-iteration; out = decode(code) * scale.
+enum DqMode { kDqFp8 = 0, kDqMx = 1, kDqNv = 2, kDqInt4 = 3 };
+
+struct DequantArgs {
+  const uint8_t* codes;
+  const void* scales;
+  const void* zp;
+  void* out;
+  int64_t n;           // elements
+  int64_t cols;
+  int block_k;         // scale run along the last axis (must be a multiple of 16)
+  int block_m;         // rows per scale (2-D block FP8), else 1
+  int64_t scale_cols;  // cols / block_k
+  int per_tensor;
+  int is_signed;
+  int scale_f16;
+};
+
+template <int OUT>
+__device__ __forceinline__ void store_out16(void* out, int64_t e0, const float* v) {
+  if constexpr (OUT == BRC_DTYPE_F32) {
+    float* o = static_cast<float*>(out) + e0;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4)
+      stg16(o + i, make_uint4(__float_as_uint(v[i]), __float_as_uint(v[i + 1]),
+                              __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3])));
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if constexpr (OUT == BRC_DTYPE_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    char* o = static_cast<char*>(out) + e0 * 2;
+    stg16(o, make_uint4(w[0], w[1], w[2], w[3]));
+    stg16(o + 16, make_uint4(w[4], w[5], w[6], w[7]));
+  }
+}
+
+template <int DQ, int FMT, int OUT>
+__global__ void __launch_bounds__(256) k_dequant(DequantArgs a) {
+  const int64_t nchunks = a.n / 16;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = c * 16;
+    const uint4 cv = ldg16(a.codes + e0);
+    const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
+    float scale = 0.f, zp = 0.f;
+    if (a.per_tensor) {
+      scale = *static_cast<const float*>(a.scales);
+    } else {
+      const int64_t row = e0 / a.cols, col = e0 - row * a.cols;
+      const int64_t si = (row / a.block_m) * a.scale_cols + col / a.block_k;
+      if constexpr (DQ == kDqFp8) scale = static_cast<const float*>(a.scales)[si];
+      else if constexpr (DQ == kDqMx) {
+        const uint32_t e = static_cast<const uint8_t*>(a.scales)[si];
+        scale = e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127);
+      } else if constexpr (DQ == kDqNv) {
+        scale = dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
+      } else {
+        if (a.scale_f16) {
+          scale = __half2float(static_cast<const __half*>(a.scales)[si]);
+          if (a.zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
+        } else {
+          scale = static_cast<const float*>(a.scales)[si];
+          if (a.zp) zp = static_cast<const float*>(a.zp)[si];
+        }
+      }
+    }
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t code = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+      float d;
+      if constexpr (DQ == kDqFp8 || DQ == kDqMx) d = dec_fp8<FMT>(code);
+      else if constexpr (DQ == kDqNv) d = dec_e2m1(code);
+      else {
+        const uint32_t lo = code & 0xFu;
+        d = (a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+        if (a.zp) d = __fsub_rn(d, zp);
+      }
+      v[i] = __fmul_rn(d, scale);
+    }
+    store_out16<OUT>(a.out, e0, v);
+  }
+}
+
+// --------------------------------------------------------------- requantize
+// NVFP4 (unpacked codes + E4M3 scales) -> MXFP8, one lane per 32-element
+// MXFP8 block. Dequantized values are exact float32 products, so this equals
+// cast(dequantize(st), MXFP8BlockScaling(fmt)).
+template <int FMT>
+__global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restrict__ codes,
+                                                          const uint8_t* __restrict__ scales,
+                                                          int64_t n_blocks, FastDiv bpr,
+                                                          uint32_t sf_col_tiles, uint8_t* out,
+                                                          uint8_t* out_scales,
+                                                          uint8_t* out_mma) {
+  constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+  for (int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; blk < n_blocks;
+       blk += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 c0 = ldg16(codes + blk * 32), c1 = ldg16(codes + blk * 32 + 16);
+    const float s0 = dec_e4m3(scales[2 * blk]), s1 = dec_e4m3(scales[2 * blk + 1]);
+    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    float f[32];
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float d = dec_e2m1((w[i >> 2] >> (8 * (i & 3))) & 0xFu);
+      f[i] = __fmul_rn(d, i < 16 ? s0 : s1);
+      am = fmax_nan(am, fabsf(f[i]));
+    }
+    am = fmax_nan(am, 1e-10f);
+    const uint32_t e = e8m0_code(__fdiv_rn(am, kMax), g_e8m0_thr);
+    out_scales[blk] = (uint8_t)e;
+    if (out_mma) {
+      const uint32_t row = fdiv((uint32_t)blk, bpr);
+      out_mma[sf_mma_offset(row, (uint32_t)blk - row * bpr.d, sf_col_tiles)] = (uint8_t)e;
+    }
+    uint32_t o[8];
+    if (isfinite(am)) {
+      const float inv = exp2i(127 - (int)e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = enc4_fp8<FMT>(__fmul_rn(f[4 * j], inv), __fmul_rn(f[4 * j + 1], inv),
+                             __fmul_rn(f[4 * j + 2], inv), __fmul_rn(f[4 * j + 3], inv));
+    } else {
+      const float act = e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t c = 0;
+        for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * j + i], act)) << (8 * i);
+        o[j] = c;
+      }
+    }
+    stg16(out + blk * 32, make_uint4(o[0], o[1], o[2], o[3]));
+    stg16(out + blk * 32 + 16, make_uint4(o[4], o[5], o[6], o[7]));
+  }
+}
+
+}  // namespace brc
+
+// ========================================================================
+// Host side: argument checks, launch configuration, C ABI.
+// ========================================================================
+using namespace brc;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool valid_dtype(int dt) { return dt == BRC_DTYPE_F32 || dt == BRC_DTYPE_BF16 || dt == BRC_DTYPE_F16; }
+bool valid_fmt(int f) { return f == BRC_FP8_E4M3 || f == BRC_FP8_E5M2; }
+bool valid_out(int dt) { return valid_dtype(dt); }
+
+int grid_for(int64_t work_items, int per_cta) {
+  const int64_t want = (work_items + per_cta - 1) / per_cta;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  return (int)(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+// Dispatch helpers: map runtime enums onto template instances.
+template <template <int, int> class F, typename... Args>
+int dispatch_dt_fmt(int dt, int fmt, Args... args) {
+  if (dt == BRC_DTYPE_F32)
+    return fmt == BRC_FP8_E4M3 ? F<BRC_DTYPE_F32, BRC_FP8_E4M3>::run(args...)
+                               : F<BRC_DTYPE_F32, BRC_FP8_E5M2>::run(args...);
+  if (dt == BRC_DTYPE_BF16)
+    return fmt == BRC_FP8_E4M3 ? F<BRC_DTYPE_BF16, BRC_FP8_E4M3>::run(args...)
+                               : F<BRC_DTYPE_BF16, BRC_FP8_E5M2>::run(args...);
+  return fmt == BRC_FP8_E4M3 ? F<BRC_DTYPE_F16, BRC_FP8_E4M3>::run(args...)
+                             : F<BRC_DTYPE_F16, BRC_FP8_E5M2>::run(args...);
+}
+
+// Launch the vectorised block kernel for block size B with LPB lanes per
+// block, choosing LPB so each lane owns 32 bytes (16 halves / 8 floats) or,
+// for big blocks, 64 bytes.
+template <int DT, int MODE, int FMT, int B>
+int launch_block_b(const BlockCastArgs& a, cudaStream_t st) {
+  constexpr int V = In<DT>::kVec;
+  constexpr int E0 = (DT == BRC_DTYPE_F32) ? 8 : 16;  // 32 bytes per lane
+  constexpr int E = (B >= 128) ? 2 * E0 : (B < E0 ? B : E0);
+  constexpr int LPB = B / E;
+  static_assert(E % V == 0 && LPB >= 1 && LPB <= 32, "bad lane split");
+  const int64_t tiles = (a.n_blocks + (32 / LPB) - 1) / (32 / LPB);
+  const int grid = grid_for(tiles, 8);
+  k_block_cast<DT, MODE, FMT, B, LPB><<<grid, 256, 0, st>>>(a);
+  return check_launch();
+}
+
+template <int DT, int MODE, int FMT>
+int launch_block(const BlockCastArgs& a, int B, cudaStream_t st) {
+  switch (B) {
+    case 16: return launch_block_b<DT, MODE, FMT, 16>(a, st);
+    case 32: return launch_block_b<DT, MODE, FMT, 32>(a, st);
+    case 64: return launch_block_b<DT, MODE, FMT, 64>(a, st);
+    case 128: return launch_block_b<DT, MODE, FMT, 128>(a, st);
+    case 256: return launch_block_b<DT, MODE, FMT, 256>(a, st);
+    default: break;
+  }
+  if (MODE == kBlockFp8 || MODE == kInt4Sym || MODE == kInt4Asym) {
+    if (a.packed && (B & 1)) return BRC_ERR_UNSUPPORTED;
+    k_block_cast_generic<DT, MODE, FMT><<<grid_for(a.n_blocks, 256), 256, 0, st>>>(a, B);
+    return check_launch();
+  }
+  return BRC_ERR_UNSUPPORTED;
+}
+
+template <int MODE, int FMT>
+int launch_block_any_dt(int dt, const BlockCastArgs& a, int B, cudaStream_t st) {
+  if (dt == BRC_DTYPE_F32) return launch_block<BRC_DTYPE_F32, MODE, FMT>(a, B, st);
+  if (dt == BRC_DTYPE_BF16) return launch_block<BRC_DTYPE_BF16, MODE, FMT>(a, B, st);
+  return launch_block<BRC_DTYPE_F16, MODE, FMT>(a, B, st);
+}
+
+// Empty inputs are valid no-ops (their data pointers may be NULL).
+bool empty_input(int64_t rows, int64_t cols, int B) {
+  return rows >= 0 && cols >= 0 && B > 0 && cols % B == 0 && rows * cols == 0;
+}
+
+int common_checks(const void* x, int dt, int64_t rows, int64_t cols, int B) {
+  if (empty_input(rows, cols, B)) return valid_dtype(dt) ? BRC_OK : BRC_ERR_DTYPE;
+  if (!x) return BRC_ERR_NULL;
+  if (!valid_dtype(dt)) return BRC_ERR_DTYPE;
+  if (rows < 0 || cols < 0 || B <= 0) return BRC_ERR_SHAPE;
+  if (cols % B != 0) return BRC_ERR_SHAPE;
+  if (!aligned16(x)) return BRC_ERR_ALIGN;
+  return BRC_OK;
+}
+
+BlockCastArgs make_args(const void* x, int64_t rows, int64_t cols, int B) {
+  BlockCastArgs a{};
+  a.x = x;
+  a.n_blocks = rows * (cols / B);
+  const int64_t bpr = cols / B;
+  a.blocks_per_row = make_fastdiv((uint32_t)(bpr > 0 ? bpr : 1));
+  a.sf_col_tiles = (uint32_t)((bpr + 3) / 4);
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+int brc_amax_reset(uint32_t* amax_bits, void* stream) {
+  if (!amax_bits) return BRC_ERR_NULL;
+  k_amax_reset<<<1, 1, 0, (cudaStream_t)stream>>>(amax_bits);
+  return check_launch();
+}
+
+int brc_amax_accumulate(const void* x, int x_dtype, int64_t n, uint32_t* amax_bits,
+                        void* stream) {
+  if (!amax_bits || (!x && n > 0)) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype)) return BRC_ERR_DTYPE;
+  if (n < 0) return BRC_ERR_SHAPE;
+  if (n == 0) return BRC_OK;
+  if (!aligned16(x)) return BRC_ERR_ALIGN;
+  const int V = x_dtype == BRC_DTYPE_F32 ? 4 : 8;
+  const int grid = grid_for(n / V + 1, 256 * 4);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (x_dtype == BRC_DTYPE_F32) k_amax<BRC_DTYPE_F32><<<grid, 256, 0, st>>>(x, n, amax_bits);
+  else if (x_dtype == BRC_DTYPE_BF16) k_amax<BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(x, n, amax_bits);
+  else k_amax<BRC_DTYPE_F16><<<grid, 256, 0, st>>>(x, n, amax_bits);
+  return check_launch();
+}
+
+}  // extern "C"
+namespace {
+template <int DT, int FMT>
+struct PerTensorApply {
+  static int run(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* codes,
+                 float* scale_out, cudaStream_t st) {
+    const double fmax = FMT == BRC_FP8_E4M3 ? 448.0 : 57344.0;
+    const float floor_scale = (float)(1e-10 / fmax);
+    const int V = In<DT>::kVec;
+    const int grid = grid_for(n / V + 1, 256 * 2);
+    k_pertensor_apply<DT, FMT><<<grid, 256, 0, st>>>(x, n, amax_bits, floor_scale, codes,
+                                                     scale_out);
+    return check_launch();
+  }
+};
+}  // namespace
+extern "C" {
+
+int brc_cast_pertensor_fp8_apply(const void* x, int x_dtype, int64_t n, int fmt,
+                                 const uint32_t* amax_bits, uint8_t* codes, float* scale_out,
+                                 void* stream) {
+  if (!amax_bits || !scale_out || ((!x || !codes) && n > 0)) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype) || !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (n < 0) return BRC_ERR_SHAPE;
+  if (n > 0 && (!aligned16(x) || !aligned16(codes))) return BRC_ERR_ALIGN;
+  return dispatch_dt_fmt<PerTensorApply>(x_dtype, fmt, x, n, amax_bits, codes, scale_out,
+                                         (cudaStream_t)stream);
+}
+
+int brc_cast_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt, uint8_t* codes,
+                           float* scale_out, uint32_t* workspace, void* stream) {
+  if (!workspace) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype) || !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  int rc = brc_amax_reset(workspace, stream);
+  if (rc) return rc;
+  rc = brc_amax_accumulate(x, x_dtype, n, workspace, stream);
+  if (rc) return rc;
+  return brc_cast_pertensor_fp8_apply(x, x_dtype, n, fmt, workspace, codes, scale_out, stream);
+}
+
+int brc_cast_block_fp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int block_k,
+                       int fmt, uint8_t* codes, float* scales, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, block_k);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (empty_input(rows, cols, block_k)) return BRC_OK;
+  if (!codes || !scales) return BRC_ERR_NULL;
+  if (!aligned16(codes)) return BRC_ERR_ALIGN;
+  BlockCastArgs a = make_args(x, rows, cols, block_k);
+  a.codes = codes;
+  a.scales = scales;
+  cudaStream_t st = (cudaStream_t)stream;
+  return fmt == BRC_FP8_E4M3 ? launch_block_any_dt<kBlockFp8, BRC_FP8_E4M3>(x_dtype, a, block_k, st)
+                             : launch_block_any_dt<kBlockFp8, BRC_FP8_E5M2>(x_dtype, a, block_k, st);
+}
+
+}  // extern "C"
+namespace {
+template <int DT, int FMT>
+struct Block2d {
+  static int run(const void* x, int64_t rows, int64_t cols, int bm, int bk, uint8_t* codes,
+                 float* scales, cudaStream_t st) {
+    constexpr int V = In<DT>::kVec;
+    if (bk % V) return BRC_ERR_UNSUPPORTED;
+    const int64_t nvec = (int64_t)bm * (bk / V);
+    if (nvec > 256 * 16) return BRC_ERR_UNSUPPORTED;
+    dim3 grid((unsigned)(cols / bk), (unsigned)(rows / bm));
+    k_block2d_cast<DT, FMT, 16><<<grid, 256, 0, st>>>(x, cols, bm, bk, codes, scales);
+    return check_launch();
+  }
+};
+}  // namespace
+extern "C" {
+
+int brc_cast_block_fp8_2d(const void* x, int x_dtype, int64_t rows, int64_t cols, int block_m,
+                          int block_k, int fmt, uint8_t* codes, float* scales, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, block_k);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (block_m <= 0 || rows % block_m) return BRC_ERR_SHAPE;
+  if (empty_input(rows, cols, block_k)) return BRC_OK;
+  if (!codes || !scales) return BRC_ERR_NULL;
+  if (!aligned16(codes)) return BRC_ERR_ALIGN;
+  if (rows / block_m > 65535 || cols / block_k > INT32_MAX) return BRC_ERR_RANGE;
+  return dispatch_dt_fmt<Block2d>(x_dtype, fmt, x, rows, cols, block_m, block_k, codes, scales,
+                                  (cudaStream_t)stream);
+}
+
+int brc_cast_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int fmt,
+                   uint8_t* codes, uint8_t* scales, uint8_t* scales_mma, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, 32);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (empty_input(rows, cols, 32)) return BRC_OK;
+  if (!codes || !scales) return BRC_ERR_NULL;
+  if (!aligned16(codes)) return BRC_ERR_ALIGN;
+  if (rows * (cols / 32) >= (1ll << 31)) return BRC_ERR_RANGE;
+  BlockCastArgs a = make_args(x, rows, cols, 32);
+  a.codes = codes;
+  a.scales = scales;
+  a.scales_mma = scales_mma;
+  cudaStream_t st = (cudaStream_t)stream;
+  return fmt == BRC_FP8_E4M3 ? launch_block_any_dt<kMxfp8, BRC_FP8_E4M3>(x_dtype, a, 32, st)
+                             : launch_block_any_dt<kMxfp8, BRC_FP8_E5M2>(x_dtype, a, 32, st);
+}
+
+int brc_cast_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t cols, uint8_t* codes,
+                   uint8_t* packed, uint8_t* scales, uint8_t* scales_mma, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, 16);
+  if (rc) return rc;
+  if (empty_input(rows, cols, 16)) return BRC_OK;
+  if (!scales || (!codes && !packed)) return BRC_ERR_NULL;
+  if ((codes && !aligned16(codes)) || (packed && !aligned16(packed))) return BRC_ERR_ALIGN;
+  if (rows * (cols / 16) >= (1ll << 31)) return BRC_ERR_RANGE;
+  BlockCastArgs a = make_args(x, rows, cols, 16);
+  a.codes = codes;
+  a.packed = packed;
+  a.scales = scales;
+  a.scales_mma = scales_mma;
+  return launch_block_any_dt<kNvfp4, 0>(x_dtype, a, 16, (cudaStream_t)stream);
+}
+
+int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int group,
+                  int is_signed, int symmetric, int scale_dtype, uint8_t* codes,
+                  uint8_t* packed, void* scales, void* zero_points, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, group);
+  if (rc) return rc;
+  if (!symmetric && is_signed) return BRC_ERR_UNSUPPORTED;
+  if (scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32) return BRC_ERR_DTYPE;
+  if (empty_input(rows, cols, group)) return BRC_OK;
+  if (!scales || (!codes && !packed)) return BRC_ERR_NULL;
+  if (!symmetric && !zero_points) return BRC_ERR_NULL;
+  if ((codes && !aligned16(codes)) || (packed && !aligned16(packed))) return BRC_ERR_ALIGN;
+  BlockCastArgs a = make_args(x, rows, cols, group);
+  a.codes = codes;
+  a.packed = packed;
+  a.scales = scales;
+  a.zp = zero_points;
+  a.is_signed = is_signed ? 1 : 0;
+  a.scale_f16 = scale_dtype == BRC_SCALE_F16;
+  cudaStream_t st = (cudaStream_t)stream;
+  return symmetric ? launch_block_any_dt<kInt4Sym, 0>(x_dtype, a, group, st)
+                   : launch_block_any_dt<kInt4Asym, 0>(x_dtype, a, group, st);
+}
+
+// ---------------------------------------------------------------- dequant
+}  // extern "C"
+namespace {
+template <int DQ, int FMT>
+int launch_dequant(const DequantArgs& a, int out_dtype, cudaStream_t st) {
+  const int grid = grid_for(a.n / 16 + 1, 256 * 2);
+  if (out_dtype == BRC_DTYPE_F32) k_dequant<DQ, FMT, BRC_DTYPE_F32><<<grid, 256, 0, st>>>(a);
+  else if (out_dtype == BRC_DTYPE_BF16) k_dequant<DQ, FMT, BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(a);
+  else k_dequant<DQ, FMT, BRC_DTYPE_F16><<<grid, 256, 0, st>>>(a);
+  return check_launch();
+}
+
+int dq_checks(const uint8_t* codes, const void* scales, void* out, int64_t n, int out_dtype) {
+  if ((!codes || !out || !scales) && n > 0) return BRC_ERR_NULL;
+  if (!valid_out(out_dtype)) return BRC_ERR_DTYPE;
+  if (n < 0 || n % 16) return BRC_ERR_SHAPE;
+  if (n > 0 && (!aligned16(codes) || !aligned16(out))) return BRC_ERR_ALIGN;
+  return BRC_OK;
+}
+}  // namespace
+extern "C" {
+
+int brc_dequant_pertensor_fp8(const uint8_t* codes, int64_t n, int fmt, const float* scale,
+                              void* out, int out_dtype, void* stream) {
+  int rc = dq_checks(codes, scale, out, n, out_dtype);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (n == 0) return BRC_OK;
+  DequantArgs a{};
+  a.codes = codes;
+  a.scales = scale;
+  a.out = out;
+  a.n = n;
+  a.cols = n;
+  a.block_k = 16;
+  a.block_m = 1;
+  a.per_tensor = 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  return fmt == BRC_FP8_E4M3 ? launch_dequant<kDqFp8, BRC_FP8_E4M3>(a, out_dtype, st)
+                             : launch_dequant<kDqFp8, BRC_FP8_E5M2>(a, out_dtype, st);
+}
+
+int brc_dequant_block_fp8(const uint8_t* codes, int64_t rows, int64_t cols, int block_m,
+                          int block_k, int fmt, const float* scales, void* out, int out_dtype,
+                          void* stream) {
+  const int64_t n = rows * cols;
+  int rc = dq_checks(codes, scales, out, n, out_dtype);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (block_k <= 0 || block_m <= 0 || cols % block_k || rows % block_m) return BRC_ERR_SHAPE;
+  if (block_k % 16) return BRC_ERR_UNSUPPORTED;
+  if (n == 0) return BRC_OK;
+  DequantArgs a{};
+  a.codes = codes;
+  a.scales = scales;
+  a.out = out;
+  a.n = n;
+  a.cols = cols;
+  a.block_k = block_k;
+  a.block_m = block_m;
+  a.scale_cols = cols / block_k;
+  cudaStream_t st = (cudaStream_t)stream;
+  return fmt == BRC_FP8_E4M3 ? launch_dequant<kDqFp8, BRC_FP8_E4M3>(a, out_dtype, st)
+                             : launch_dequant<kDqFp8, BRC_FP8_E5M2>(a, out_dtype, st);
+}
+
+int brc_dequant_mxfp8(const uint8_t* codes, int64_t rows, int64_t cols, int fmt,
+                      const uint8_t* scales, void* out, int out_dtype, void* stream) {
+  const int64_t n = rows * cols;
+  int rc = dq_checks(codes, scales, out, n, out_dtype);
+  if (rc) return rc;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (cols % 32) return BRC_ERR_SHAPE;
+  if (n == 0) return BRC_OK;
+  DequantArgs a{};
+  a.codes = codes;
+  a.scales = scales;
+  a.out = out;
+  a.n = n;
+  a.cols = cols;
+  a.block_k = 32;
+  a.block_m = 1;
+  a.scale_cols = cols / 32;
+  cudaStream_t st = (cudaStream_t)stream;
+  return fmt == BRC_FP8_E4M3 ? launch_dequant<kDqMx, BRC_FP8_E4M3>(a, out_dtype, st)
+                             : launch_dequant<kDqMx, BRC_FP8_E5M2>(a, out_dtype, st);
+}
+
+int brc_dequant_nvfp4(const uint8_t* codes, int64_t rows, int64_t cols, const uint8_t* scales,
+                      void* out, int out_dtype, void* stream) {
+  const int64_t n = rows * cols;
+  int rc = dq_checks(codes, scales, out, n, out_dtype);
+  if (rc) return rc;
+  if (cols % 16) return BRC_ERR_SHAPE;
+  if (n == 0) return BRC_OK;
+  DequantArgs a{};
+  a.codes = codes;
+  a.scales = scales;
+  a.out = out;
+  a.n = n;
+  a.cols = cols;
+  a.block_k = 16;
+  a.block_m = 1;
+  a.scale_cols = cols / 16;
+  return launch_dequant<kDqNv, 0>(a, out_dtype, (cudaStream_t)stream);
+}
+
+int brc_dequant_int4(const uint8_t* codes, int64_t rows, int64_t cols, int group, int is_signed,
+                     int scale_dtype, const void* scales, const void* zero_points, void* out,
+                     int out_dtype, void* stream) {
+  const int64_t n = rows * cols;
+  int rc = dq_checks(codes, scales, out, n, out_dtype);
+  if (rc) return rc;
+  if (group <= 0 || cols % group) return BRC_ERR_SHAPE;
+  if (group % 16) return BRC_ERR_UNSUPPORTED;
+  if (scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32) return BRC_ERR_DTYPE;
+  if (n == 0) return BRC_OK;
+  DequantArgs a{};
+  a.codes = codes;
+  a.scales = scales;
+  a.zp = zero_points;
+  a.out = out;
+  a.n = n;
+  a.cols = cols;
+  a.block_k = group;
+  a.block_m = 1;
+  a.scale_cols = cols / group;
+  a.is_signed = is_signed ? 1 : 0;
+  a.scale_f16 = scale_dtype == BRC_SCALE_F16;
+  return launch_dequant<kDqInt4, 0>(a, out_dtype, (cudaStream_t)stream);
+}
+
+int brc_requant_nvfp4_to_mxfp8(const uint8_t* codes, const uint8_t* scales, int64_t rows,
+                               int64_t cols, int fmt, uint8_t* codes_out, uint8_t* scales_out,
+                               uint8_t* scales_mma_out, void* stream) {
+  if (!codes || !scales || !codes_out || !scales_out) return BRC_ERR_NULL;
+  if (!valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (rows < 0 || cols < 0 || cols % 32) return BRC_ERR_SHAPE;
+  if (!aligned16(codes) || !aligned16(codes_out)) return BRC_ERR_ALIGN;
+  const int64_t n_blocks = rows * (cols / 32);
+  if (n_blocks >= (1ll << 31)) return BRC_ERR_RANGE;
+  if (n_blocks == 0) return BRC_OK;
+  const int64_t bpr = cols / 32;
+  const FastDiv f = make_fastdiv((uint32_t)bpr);
+  const uint32_t tiles = (uint32_t)((bpr + 3) / 4);
+  const int grid = grid_for(n_blocks, 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (fmt == BRC_FP8_E4M3)
+    k_requant_nv_to_mx<BRC_FP8_E4M3><<<grid, 256, 0, st>>>(codes, scales, n_blocks, f, tiles,
+                                                            codes_out, scales_out, scales_mma_out);
+  else
+    k_requant_nv_to_mx<BRC_FP8_E5M2><<<grid, 256, 0, st>>>(codes, scales, n_blocks, f, tiles,
+                                                            codes_out, scales_out, scales_mma_out);
+  return check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,543 @@
+// Tensor-core scaled GEMMs for sm_100a (tcgen05 + TMA + TMEM).
+//
+//   D[M, N] = A[M, K] * B[N, K]^T, both operands K-major ("NT"), FP32
+//   accumulation in TMEM, output float32 / bfloat16 / float16.
+//
+// Kinds:
+//   kPerTensor : kind::f8f6f4, E4M3/E5M2 codes, epilogue multiplies by the
+//                two per-tensor scales (DelayedScaling / Float8CurrentScaling).
+//   kMxfp8     : kind::mxf8f6f4.block_scale, UE8M0 scale per 32 K-elements.
+//   kNvfp4     : kind::mxf4nvf4.block_scale.scale_vec::4X, packed E2M1 codes,
+//                UE4M3 scale per 16 K-elements.
+// Block scales are consumed in the 512-byte "atom" layout the casts write
+// (128 rows x 4 scale columns per atom).
+//
+// One persistent CTA per SM, 10 warps:
+//   warp 0    TMA producer (operand tiles + scale atoms) into a 4-stage ring
+//   warp 1    TMEM owner and MMA issuer (one thread)
+//   warps 2-9 epilogue: each pulls 128 accumulator columns of 32 rows from
+//             TMEM into registers, releases the accumulator, then scales,
+//             converts and stores while the next tile's MMAs run.
+// Tile 128 x 256 x (128 bytes of K per stage). Tiles are visited in groups of
+// 16 M-blocks so the A rows of a group stay in L2 while B streams.
+//
+// Every wait is bounded (sm100::mbar_wait); on a timeout the kernel records
+// BRC_GEMM_STATUS_TIMEOUT, drains its own copies and MMAs, frees TMEM and
+// returns.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "breccia_b200.h"
+#include "launch.h"
+#include "sm100.cuh"
+
+namespace brc {
+
+__device__ uint32_t g_gemm_status = 0;  // sticky: bit 0 = a bounded wait timed out
+
+namespace gemm {
+
+using namespace sm100;
+
+enum Kind { kPerTensor = 0, kMxfp8 = 1, kNvfp4 = 2 };
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BKB = 128;  // K bytes per stage (one 128-byte swizzle row)
+constexpr int STAGES = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int GROUP_M = 16;
+constexpr uint32_t A_BYTES = BM * BKB;  // 16 KB
+constexpr uint32_t B_BYTES = BN * BKB;  // 32 KB
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_COL = 0;
+constexpr uint32_t SF_COL = 256;
+
+template <int KIND>
+struct SfCfg {
+  // scale atoms per stage: A (128 rows) and B per 128-row half
+  static constexpr uint32_t kAtomsK = KIND == kNvfp4 ? 4 : (KIND == kMxfp8 ? 1 : 0);
+  static constexpr uint32_t A_SF = 512 * kAtomsK;
+  static constexpr uint32_t B_SF = 2 * 512 * kAtomsK;
+  static constexpr uint32_t SFA_COLS = 4 * kAtomsK;  // TMEM columns per stage
+  static constexpr uint32_t SFB_COLS = 8 * kAtomsK;
+};
+
+template <int KIND>
+struct Smem {
+  static constexpr uint32_t kA = 0;
+  static constexpr uint32_t kB = kA + STAGES * A_BYTES;
+  static constexpr uint32_t kSfA = kB + STAGES * B_BYTES;
+  static constexpr uint32_t kSfB = kSfA + STAGES * SfCfg<KIND>::A_SF;
+  static constexpr uint32_t kBar = kSfB + STAGES * SfCfg<KIND>::B_SF;
+  static constexpr uint32_t kMisc = kBar + 8 * (2 * STAGES + 3);
+  static constexpr uint32_t kTotal = kMisc + 16;
+  static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
+};
+
+struct Params {
+  int M, N, K;           // K in elements
+  int num_m, num_n, num_kb;
+  const float* a_scale;  // per-tensor scales (kPerTensor)
+  const float* b_scale;
+  const uint8_t* sfa;    // scale atoms (block-scaled kinds)
+  const uint8_t* sfb;
+  uint32_t sf_col_tiles;  // atoms per 128-row group along K
+  int sfb_row_atoms;      // ceil(N / 128)
+  void* d;
+  int64_t ldd;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
+  const int per_group = GROUP_M * p.num_n;
+  const int g = tile / per_group;
+  const int first = g * GROUP_M;
+  const int gsize = min(p.num_m - first, GROUP_M);
+  const int r = tile - g * per_group;
+  mb = first + r % gsize;
+  nb = r / gsize;
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_row_chunk(void* d, int64_t ldd, int row, int col0,
+                                                int N, const float* v, int count) {
+  // `count` consecutive columns starting at col0 (count % 8 == 0), clipped at N.
+  if constexpr (OUT == BRC_DTYPE_F32) {
+    float* out = static_cast<float*>(d) + (int64_t)row * ldd + col0;
+#pragma unroll
+    for (int c = 0; c < count; c += 4)
+      if (col0 + c < N)
+        *reinterpret_cast<float4*>(out + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+  } else {
+    __half* out = static_cast<__half*>(d) + (int64_t)row * ldd + col0;
+#pragma unroll
+    for (int c = 0; c < count; c += 8) {
+      if (col0 + c < N) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if constexpr (OUT == BRC_DTYPE_BF16) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[c + 2 * i], v[c + 2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+          } else {
+            const __half2 h = __floats2half2_rn(v[c + 2 * i], v[c + 2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
+template <int KIND, int AFMT, int BFMT, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+           const Params p) {
+  using SF = SfCfg<KIND>;
+  using L = Smem<KIND>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain = tmem_empty + 1;
+  uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, kEpiWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;  // per-stage bits for the drain
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          uint32_t bytes = A_BYTES + B_BYTES;
+          const bool b_hi = KIND != kPerTensor && (2 * nb + 1) < p.sfb_row_atoms;
+          if constexpr (KIND != kPerTensor) bytes += SF::A_SF + (b_hi ? SF::B_SF : SF::B_SF / 2);
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d(smem + L::kA + stage * A_BYTES, &tmap_a, kb * BKB, mb * BM, &full[stage]);
+          tma_load_2d(smem + L::kB + stage * B_BYTES, &tmap_b, kb * BKB, nb * BN, &full[stage]);
+          if constexpr (KIND != kPerTensor) {
+            const uint32_t kcol = (uint32_t)kb * SF::kAtomsK;
+            bulk_load(smem + L::kSfA + stage * SF::A_SF,
+                      p.sfa + ((size_t)mb * p.sf_col_tiles + kcol) * 512, SF::A_SF, &full[stage]);
+            bulk_load(smem + L::kSfB + stage * SF::B_SF,
+                      p.sfb + ((size_t)(2 * nb) * p.sf_col_tiles + kcol) * 512, SF::B_SF / 2,
+                      &full[stage]);
+            if (b_hi)
+              bulk_load(smem + L::kSfB + stage * SF::B_SF + SF::B_SF / 2,
+                        p.sfb + ((size_t)(2 * nb + 1) * p.sf_col_tiles + kcol) * 512,
+                        SF::B_SF / 2, &full[stage]);
+          }
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // wait for this thread's copies in flight before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, abort_flag, p.status, 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(smem + L::kB + stage * B_BYTES);
+          uint32_t sfa_col = 0, sfb_col = 0;
+          if constexpr (KIND != kPerTensor) {
+            sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+            sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
+            const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
+            const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
+#pragma unroll
+            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+              tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+              tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+              tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+            }
+          }
+#pragma unroll
+          for (uint32_t k = 0; k < 4; ++k) {
+            const uint64_t ad = desc_kmajor_sw128(a_addr + 32 * k);
+            const uint64_t bd = desc_kmajor_sw128(b_addr + 32 * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (KIND == kPerTensor) {
+              mma_f8f6f4(tmem + ACC_COL, ad, bd, idesc_f8f6f4(AFMT, BFMT, BM, BN), acc);
+            } else if constexpr (KIND == kMxfp8) {
+              mma_mxf8f6f4(tmem + ACC_COL, ad, bd,
+                           idesc_block_scaled(AFMT, BFMT, BM, BN, 1u, k, k),
+                           sfa_col | (k << 30), sfb_col | (k << 30), acc);
+            } else {
+              mma_mxf4nvf4_4x(tmem + ACC_COL, ad, bd, idesc_block_scaled(1u, 1u, BM, BN, 0u, 0u, 0u),
+                              sfa_col + 4 * k, sfb_col + 8 * k, acc);
+            }
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tmem_full);
+        acc_phase ^= 1u;
+      }
+      // every MMA this thread issued has completed before TMEM is freed
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+    const int half = ew / 4;          // which 128 accumulator columns
+    float scale = 1.f;
+    if constexpr (KIND == kPerTensor) scale = __fmul_rn(*p.a_scale, *p.b_scale);
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      if (!mbar_wait(tmem_full, acc_phase, abort_flag, p.status, 1u)) break;
+      acc_phase ^= 1u;
+      tc_fence_after();
+      uint32_t r[4][32];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + ACC_COL + 128 * half;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_empty);
+      const int row = mb * BM + 32 * quad + lane;
+      const int col0 = nb * BN + 128 * half;
+      if (row < p.M) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __uint_as_float(r[c][i]);
+            if constexpr (KIND == kPerTensor) v[i] = __fmul_rn(v[i], scale);
+          }
+          store_row_chunk<OUT>(p.d, p.ldd, row, col0 + 32 * c, p.N, v, 32);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Row-major uint8 matrix [rows, row_bytes] -> box [box_rows, 128 bytes], 128B swizzle.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes,
+              uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return BRC_ERR_CUDA;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {BKB, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BRC_OK : BRC_ERR_CUDA;
+}
+
+template <int KIND, int AFMT, int BFMT, int OUT>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  auto kern = k_gemm<KIND, AFMT, BFMT, OUT>;
+  const int smem = (int)Smem<KIND>::kAlloc;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return BRC_ERR_CUDA;
+  if (!configured[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (rc) return rc;
+    configured[dev] = true;
+  }
+  const int tiles = p.num_m * p.num_n;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return check_launch();
+}
+
+template <int KIND, int AFMT, int BFMT>
+int launch_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+               cudaStream_t st) {
+  if (out_dtype == BRC_DTYPE_F32) return launch<KIND, AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, p, st);
+  if (out_dtype == BRC_DTYPE_BF16) return launch<KIND, AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, p, st);
+  return launch<KIND, AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, p, st);
+}
+
+int check_common(const void* a, const void* b, void* d, int M, int N, int K, int out_dtype,
+                 int k_multiple) {
+  if (!a || !b || !d) return BRC_ERR_NULL;
+  if (M < 0 || N < 0 || K < 0) return BRC_ERR_SHAPE;
+  if (out_dtype != BRC_DTYPE_F32 && out_dtype != BRC_DTYPE_BF16 && out_dtype != BRC_DTYPE_F16)
+    return BRC_ERR_DTYPE;
+  if (K % k_multiple || N % 16) return BRC_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(d)) & 15)
+    return BRC_ERR_ALIGN;
+  return BRC_OK;
+}
+
+Params base_params(int M, int N, int K, int k_per_stage, void* d) {
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m = (M + BM - 1) / BM;
+  p.num_n = (N + BN - 1) / BN;
+  p.num_kb = K / k_per_stage;
+  p.d = d;
+  p.ldd = N;
+  p.status = nullptr;
+  return p;
+}
+
+}  // namespace gemm
+}  // namespace brc
+
+using namespace brc;
+using namespace brc::gemm;
+
+namespace {
+uint32_t* status_word() {
+  uint32_t* p = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_gemm_status) != cudaSuccess)
+    return nullptr;
+  return p;
+}
+}  // namespace
+
+extern "C" {
+
+int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                           int b_fmt, const float* a_scale, const float* b_scale, void* d,
+                           int d_dtype, void* stream) {
+  int rc = check_common(a, b, d, M, N, K, d_dtype, BKB);
+  if (rc) return rc;
+  if (!a_scale || !b_scale) return BRC_ERR_NULL;
+  if ((a_fmt != BRC_FP8_E4M3 && a_fmt != BRC_FP8_E5M2) ||
+      (b_fmt != BRC_FP8_E4M3 && b_fmt != BRC_FP8_E5M2))
+    return BRC_ERR_DTYPE;
+  if ((int64_t)M * N == 0) return BRC_OK;
+  if (K == 0) return BRC_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
+  if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
+  Params p = base_params(M, N, K, BKB, d);
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.status = status_word();
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+    return launch_out<kPerTensor, 0, 0>(d_dtype, ta, tb, p, st);
+  if (a_fmt == BRC_FP8_E4M3) return launch_out<kPerTensor, 0, 1>(d_dtype, ta, tb, p, st);
+  if (b_fmt == BRC_FP8_E4M3) return launch_out<kPerTensor, 1, 0>(d_dtype, ta, tb, p, st);
+  return launch_out<kPerTensor, 1, 1>(d_dtype, ta, tb, p, st);
+}
+
+int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                   int b_fmt, const uint8_t* a_sf_mma, const uint8_t* b_sf_mma, void* d,
+                   int d_dtype, void* stream) {
+  int rc = check_common(a, b, d, M, N, K, d_dtype, BKB);
+  if (rc) return rc;
+  if (!a_sf_mma || !b_sf_mma) return BRC_ERR_NULL;
+  if ((a_fmt != BRC_FP8_E4M3 && a_fmt != BRC_FP8_E5M2) ||
+      (b_fmt != BRC_FP8_E4M3 && b_fmt != BRC_FP8_E5M2))
+    return BRC_ERR_DTYPE;
+  if (((reinterpret_cast<uintptr_t>(a_sf_mma) | reinterpret_cast<uintptr_t>(b_sf_mma)) & 15))
+    return BRC_ERR_ALIGN;
+  if ((int64_t)M * N == 0) return BRC_OK;
+  if (K == 0) return BRC_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
+  if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
+  Params p = base_params(M, N, K, BKB, d);
+  p.sfa = a_sf_mma;
+  p.sfb = b_sf_mma;
+  p.sf_col_tiles = (uint32_t)((K / 32 + 3) / 4);
+  p.sfb_row_atoms = (N + 127) / 128;
+  p.status = status_word();
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+    return launch_out<kMxfp8, 0, 0>(d_dtype, ta, tb, p, st);
+  if (a_fmt == BRC_FP8_E4M3) return launch_out<kMxfp8, 0, 1>(d_dtype, ta, tb, p, st);
+  if (b_fmt == BRC_FP8_E4M3) return launch_out<kMxfp8, 1, 0>(d_dtype, ta, tb, p, st);
+  return launch_out<kMxfp8, 1, 1>(d_dtype, ta, tb, p, st);
+}
+
+int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int N, int K,
+                   const uint8_t* a_sf_mma, const uint8_t* b_sf_mma, void* d, int d_dtype,
+                   void* stream) {
+  int rc = check_common(a_packed, b_packed, d, M, N, K, d_dtype, 2 * BKB);
+  if (rc) return rc;
+  if (!a_sf_mma || !b_sf_mma) return BRC_ERR_NULL;
+  if (((reinterpret_cast<uintptr_t>(a_sf_mma) | reinterpret_cast<uintptr_t>(b_sf_mma)) & 15))
+    return BRC_ERR_ALIGN;
+  if ((int64_t)M * N == 0) return BRC_OK;
+  if (K == 0) return BRC_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, a_packed, M, K / 2, BM))) return rc;
+  if ((rc = make_tmap(&tb, b_packed, N, K / 2, BN))) return rc;
+  Params p = base_params(M, N, K, 2 * BKB, d);
+  p.sfa = a_sf_mma;
+  p.sfb = b_sf_mma;
+  p.sf_col_tiles = (uint32_t)((K / 16 + 3) / 4);
+  p.sfb_row_atoms = (N + 127) / 128;
+  p.status = status_word();
+  return launch_out<kNvfp4, 0, 0>(d_dtype, ta, tb, p, (cudaStream_t)stream);
+}
+
+int brc_gemm_status(int reset) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess) return BRC_ERR_CUDA;
+  if (reset) {
+    const uint32_t z = 0;
+    if (cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z)) != cudaSuccess) return BRC_ERR_CUDA;
+  }
+  return (int)v;
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+"""Install this backend behind the real ``breccia`` package.
+
+breccia has no registry: its public functions are plain module attributes
+(``src/breccia/__init__.py:23`` re-exports ``cast, dequantize, requantize,
+matmul`` from ``breccia.kernels.reference``; ``breccia/autograd.py:47``
+imports ``cast`` and ``dequantize`` by name). ``install()`` rebinds each of
+those names to a wrapper that sends CUDA torch inputs to breccia_b200 and
+calls breccia's original function for everything else (NumPy, CPU torch,
+JAX, MLX). ``uninstall()`` restores the originals.
+"""
+
+from __future__ import annotations
+
+import functools
+import importlib
+
+_SITES = [
+    ("breccia", ("cast", "dequantize", "requantize", "matmul")),
+    ("breccia.kernels.reference", ("cast", "dequantize", "requantize", "matmul")),
+    ("breccia.kernels.reference.cast", ("cast", "dequantize", "requantize")),
+    ("breccia.kernels.reference.matmul", ("dequantize",)),
+    ("breccia.autograd", ("cast", "dequantize")),
+]
+_saved: dict = {}
+
+
+def _on_cuda(obj) -> bool:
+    import torch
+    if isinstance(obj, torch.Tensor):
+        return obj.is_cuda
+    data = getattr(obj, "data", None)
+    return isinstance(data, torch.Tensor) and data.is_cuda and hasattr(obj, "recipe")
+
+
+def _wrap(name, original):
+    from . import api
+
+    ours = getattr(api, name)
+
+    @functools.wraps(original)
+    def dispatch(*args, **kwargs):
+        if name == "matmul":
+            a, b = args[0], args[1]
+            if _on_cuda(a) or _on_cuda(b):
+                return ours(*args, **kwargs)
+        elif args and _on_cuda(args[0]):
+            return ours(*args, **kwargs)
+        return original(*args, **kwargs)
+
+    dispatch.__breccia_b200__ = True
+    return dispatch
+
+
+def install() -> None:
+    """Route breccia's cast/dequantize/requantize/matmul for CUDA tensors to
+    this backend. Idempotent."""
+    for modname, names in _SITES:
+        mod = importlib.import_module(modname)
+        for name in names:
+            fn = getattr(mod, name, None)
+            if fn is None or getattr(fn, "__breccia_b200__", False):
+                continue
+            _saved[(modname, name)] = fn
+            setattr(mod, name, _wrap(name, fn))
+
+
+def uninstall() -> None:
+    """Restore breccia's original functions."""
+    for (modname, name), fn in list(_saved.items()):
+        setattr(importlib.import_module(modname), name, fn)
+        del _saved[(modname, name)]

@@ -1,0 +1,207 @@
+/*
+ * breccia_b200 -- C ABI of the B200 (sm_100a) backend for breccia's hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream). Calls are
+ * stream-ordered and asynchronous: they validate arguments on the host,
+ * enqueue kernels and return. The library allocates nothing and frees
+ * nothing: the caller owns every output and workspace buffer.
+ *
+ * Return value: BRC_OK (0) or a negative BRC_ERR_* status. On BRC_ERR_CUDA,
+ * brc_last_cuda_error() gives the cudaError_t of the failing call on this
+ * thread.
+ *
+ * Numerics follow the NumPy path of jvoltci/breccia v0.1.3 bit for bit
+ * (codes and scales): round-to-nearest with ties toward zero for FP8/FP4
+ * codes, IEEE float32 division by the scale, NumPy's float32 log2 for E8M0
+ * scales, NumPy half-to-even rounding for INT4.
+ *
+ * "Reference:" lines name the function of jvoltci/breccia (path within that
+ * project) that each entry point replaces for CUDA tensors.
+ */
+#ifndef BRECCIA_B200_H
+#define BRECCIA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- enums */
+enum { BRC_DTYPE_F32 = 0, BRC_DTYPE_BF16 = 1, BRC_DTYPE_F16 = 2 };
+enum { BRC_FP8_E4M3 = 0, BRC_FP8_E5M2 = 1 };
+enum { BRC_SCALE_F16 = 0, BRC_SCALE_F32 = 1 };
+
+enum {
+  BRC_OK = 0,
+  BRC_ERR_NULL = -1,        /* a required pointer is NULL */
+  BRC_ERR_SHAPE = -2,       /* sizes inconsistent (e.g. cols % block != 0) */
+  BRC_ERR_ALIGN = -3,       /* a pointer is not 16-byte aligned */
+  BRC_ERR_DTYPE = -4,       /* unknown dtype / format enum */
+  BRC_ERR_UNSUPPORTED = -5, /* valid request this build does not handle */
+  BRC_ERR_CUDA = -6,        /* a CUDA runtime call or launch failed */
+  BRC_ERR_TIMEOUT = -7,     /* a device-side bounded wait gave up */
+  BRC_ERR_RANGE = -8        /* a size exceeds a documented limit */
+};
+
+/* Human-readable name of a status code (static string). */
+const char* brc_status_string(int status);
+/* cudaError_t of the last BRC_ERR_CUDA on the calling thread (0 if none). */
+int brc_last_cuda_error(void);
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int brc_version(void);
+
+/* ======================================================= casts: per-tensor
+ * DelayedScaling / Float8CurrentScaling.
+ * Reference: src/breccia/kernels/reference/cast.py:364-373 (_cast_per_tensor_fp8)
+ *            and src/breccia/kernels/reference/_utils.py:34-37 (tensor_amax).
+ *
+ * The global amax lives in a caller-provided device word `amax_bits` holding
+ * the float32 bit pattern of max|x| (positive floats order like unsigned
+ * integers; NaN orders above +inf, so NaN propagates).
+ *   brc_amax_reset       : *amax_bits = 0
+ *   brc_amax_accumulate  : *amax_bits = max(*amax_bits, bits(max|x|)) (atomic)
+ *   brc_cast_pertensor_fp8_apply : scale = float32(max(amax, 1e-10) / fmt_max)
+ *       computed as the reference does (float64 floor), codes = encode(x / scale),
+ *       *scale_out = scale.
+ * Sharded use: accumulate on each rank's shard, all-reduce(MAX) the word as an
+ * unsigned 32-bit integer, then apply.
+ */
+int brc_amax_reset(uint32_t* amax_bits, void* stream);
+int brc_amax_accumulate(const void* x, int x_dtype, int64_t n, uint32_t* amax_bits,
+                        void* stream);
+int brc_cast_pertensor_fp8_apply(const void* x, int x_dtype, int64_t n, int fmt,
+                                 const uint32_t* amax_bits, uint8_t* codes,
+                                 float* scale_out, void* stream);
+/* reset + accumulate + apply in one call; `workspace` is one device word. */
+int brc_cast_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt, uint8_t* codes,
+                           float* scale_out, uint32_t* workspace, void* stream);
+
+/* ======================================================= casts: block FP8
+ * Float8BlockScaling: one float32 scale per `block_k` run of the last axis.
+ * Reference: src/breccia/kernels/reference/cast.py:384-404 (_cast_block_fp8),
+ *            src/breccia/kernels/reference/_utils.py:11-31 (block_amax).
+ * x is (rows, cols) row-major; codes (rows, cols); scales (rows, cols/block_k).
+ */
+int brc_cast_block_fp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int block_k,
+                       int fmt, uint8_t* codes, float* scales, void* stream);
+
+/* block_m x block_k tiles (the 128x128 DeepSeek-v3 weight layout, which the
+ * reference type system can describe as PerBlockMN(block_m, block_k) but the
+ * reference cannot produce): the same arithmetic as _cast_block_fp8 over 2-D
+ * tiles. scales is (rows/block_m, cols/block_k). */
+int brc_cast_block_fp8_2d(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                          int block_m, int block_k, int fmt, uint8_t* codes, float* scales,
+                          void* stream);
+
+/* ======================================================= casts: MXFP8
+ * MXFP8BlockScaling: 1x32 blocks, E8M0 scale.
+ * Reference: src/breccia/kernels/reference/cast.py:420-446 (_cast_mxfp8),
+ *            src/breccia/kernels/reference/_utils.py:40-56 (E8M0 helpers).
+ * scales: (rows, cols/32) uint8, the reference layout.
+ * scales_mma (optional, may be NULL): the same scales in the tcgen05
+ * block-scale layout: 512-byte atoms of 128 rows x 4 scale columns, atom
+ * (r/128, c/4) at ((r/128) * (ceil(cols/32/4)) + c/4) * 512, byte
+ * (r%32)*16 + ((r/32)%4)*4 + c%4 within it; rows padded to 128 and scale
+ * columns to 4 (padding is not written; callers zero it once).
+ */
+int brc_cast_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int fmt,
+                   uint8_t* codes, uint8_t* scales, uint8_t* scales_mma, void* stream);
+
+/* ======================================================= casts: NVFP4
+ * NVFP4BlockScaling: 1x16 blocks, E4M3 scale (division uses max(scale, 2^-9)).
+ * Reference: src/breccia/kernels/reference/cast.py:468-496 (_cast_nvfp4).
+ * codes (optional): one E2M1 code per byte (low nibble), the reference layout.
+ * packed (optional): two codes per byte, element 2i in the LOW nibble (the
+ *   tcgen05 / cuBLAS operand order; note breccia's pack_nibbles puts element
+ *   2i in the HIGH nibble).
+ * scales: (rows, cols/16) uint8 E4M3 codes. scales_mma: as for MXFP8.
+ */
+int brc_cast_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t cols, uint8_t* codes,
+                   uint8_t* packed, uint8_t* scales, uint8_t* scales_mma, void* stream);
+
+/* ======================================================= casts: INT4
+ * INT4Scaling, symmetric (signed or unsigned) or asymmetric (zero point).
+ * Reference: src/breccia/kernels/reference/cast.py:516-571 (_cast_int4).
+ * scales / zero_points: (rows, cols/group) in scale_dtype (BRC_SCALE_F16 for
+ * "fp16"; BRC_SCALE_F32 for "fp32" and for "bf16", which the reference
+ * stores as float32). zero_points is required iff !symmetric.
+ * codes (optional): one code per byte (low nibble). packed (optional): two
+ * per byte, element 2i in the LOW nibble.
+ */
+int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int group,
+                  int is_signed, int symmetric, int scale_dtype, uint8_t* codes,
+                  uint8_t* packed, void* scales, void* zero_points, void* stream);
+
+/* ======================================================= dequantize
+ * out = decode(code) * scale (asymmetric INT4: (code - zp) * scale), written as
+ * float32 (the reference's dtype) or, as an extension, bf16/f16.
+ * Reference: src/breccia/kernels/reference/cast.py:376-378, 407-414, 449-459,
+ *            499-506, 574-586.
+ */
+int brc_dequant_pertensor_fp8(const uint8_t* codes, int64_t n, int fmt, const float* scale,
+                              void* out, int out_dtype, void* stream);
+/* block_m = 1 for the 1 x block_k layout; scales (rows/block_m, cols/block_k). */
+int brc_dequant_block_fp8(const uint8_t* codes, int64_t rows, int64_t cols, int block_m,
+                          int block_k, int fmt, const float* scales, void* out,
+                          int out_dtype, void* stream);
+int brc_dequant_mxfp8(const uint8_t* codes, int64_t rows, int64_t cols, int fmt,
+                      const uint8_t* scales, void* out, int out_dtype, void* stream);
+int brc_dequant_nvfp4(const uint8_t* codes, int64_t rows, int64_t cols,
+                      const uint8_t* scales, void* out, int out_dtype, void* stream);
+int brc_dequant_int4(const uint8_t* codes, int64_t rows, int64_t cols, int group,
+                     int is_signed, int scale_dtype, const void* scales,
+                     const void* zero_points, void* out, int out_dtype, void* stream);
+
+/* ======================================================= requantize
+ * NVFP4 -> MXFP8 in one pass (no float32 round trip through memory); equal to
+ * cast(dequantize(st), MXFP8BlockScaling(fmt)).
+ * Reference: src/breccia/kernels/reference/cast.py:339-346 (requantize).
+ */
+int brc_requant_nvfp4_to_mxfp8(const uint8_t* codes, const uint8_t* scales, int64_t rows,
+                               int64_t cols, int fmt, uint8_t* codes_out,
+                               uint8_t* scales_out, uint8_t* scales_mma_out, void* stream);
+
+/* ======================================================= scaled GEMMs
+ * D[M, N] = A[M, K] * B[N, K]^T on the tcgen05 tensor cores with float32
+ * accumulation; both operands K-major (B is the weight in nn.Linear
+ * orientation, i.e. the cast of W^T for a (K, N) weight W). D is row-major
+ * (ldd = N) in BRC_DTYPE_F32 / BF16 / F16. N % 16 == 0.
+ * Reference: src/breccia/kernels/reference/matmul.py:42-133 (dequantize both
+ * operands, float32 matmul) and, for the per-tensor kind,
+ * src/breccia/kernels/triton/scaled_matmul.py:152-257 (scaled_matmul_triton).
+ */
+/* Per-tensor FP8 (DelayedScaling / Float8CurrentScaling): codes E4M3 / E5M2,
+ * D = (A_codes @ B_codes^T) * a_scale * b_scale with the scales read from
+ * device memory (0-d tensors). K % 128 == 0. */
+int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                           int b_fmt, const float* a_scale, const float* b_scale, void* d,
+                           int d_dtype, void* stream);
+/* MXFP8: scales in the tcgen05 layout written by brc_cast_mxfp8 (scales_mma)
+ * for A (M rows) and B (N rows). K % 128 == 0. */
+int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                   int b_fmt, const uint8_t* a_sf_mma, const uint8_t* b_sf_mma, void* d,
+                   int d_dtype, void* stream);
+/* NVFP4: packed E2M1 codes (element 2i in the low nibble, as brc_cast_nvfp4
+ * writes them; K/2 bytes per row) and E4M3 scales in the tcgen05 layout.
+ * K % 256 == 0. */
+int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int N, int K,
+                   const uint8_t* a_sf_mma, const uint8_t* b_sf_mma, void* d, int d_dtype,
+                   void* stream);
+/* Sticky device status of the GEMM kernels on the current device (bit 0: a
+ * bounded wait timed out and the kernel returned early). Synchronous. */
+int brc_gemm_status(int reset);
+
+/* ======================================================= diagnostics
+ * Writes, for each i, the float32 quotient x[i] / s[i] as the cast kernels
+ * compute it (correctly rounded reciprocal refined by one FMA residual step)
+ * and as IEEE division computes it, for self-tests. No reference counterpart.
+ */
+int brc_selftest_division(const float* x, const float* s, int64_t n, float* q_fast,
+                          float* q_ieee, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BRECCIA_B200_H */

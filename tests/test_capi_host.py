@@ -1,0 +1,91 @@
+"""C ABI: the library loads without a GPU, exports exactly what the header
+declares, and rejects bad arguments on the host before touching CUDA."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from breccia_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for fn in os.listdir(inc):
+        if fn.endswith(".h"):
+            text = open(os.path.join(inc, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names |= set(re.findall(r"\b(brc_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    declared = _declared()
+    assert declared, "no declarations found"
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_declared_symbol():
+    assert _declared() == set(_lib.PROTOTYPES)
+
+
+def test_status_strings():
+    L = _lib.lib()
+    assert L.brc_status_string(0) == b"ok"
+    assert L.brc_status_string(-2) == b"inconsistent sizes"
+    assert L.brc_version() >= 100
+
+
+def _buf(n=64):
+    # host memory, 16-byte aligned: the checks below fail before any CUDA call
+    raw = (ctypes.c_uint8 * (n + 16))()
+    addr = ctypes.addressof(raw)
+    return raw, addr + (-addr % 16)
+
+
+def test_null_pointers_rejected():
+    L = _lib.lib()
+    _, p = _buf()
+    assert L.brc_cast_block_fp8(None, 0, 4, 128, 128, 0, p, p, None) == _lib.BRC_ERR_NULL
+    assert L.brc_cast_mxfp8(p, 0, 4, 64, 0, None, p, None, None) == _lib.BRC_ERR_NULL
+    assert L.brc_cast_nvfp4(p, 0, 4, 64, None, None, p, None, None) == _lib.BRC_ERR_NULL
+    # asymmetric INT4 needs a zero-point buffer
+    assert L.brc_cast_int4(p, 0, 4, 128, 128, 0, 0, 0, p, None, p, None, None) == _lib.BRC_ERR_NULL
+
+
+def test_shapes_dtypes_alignment_rejected():
+    L = _lib.lib()
+    _, p = _buf()
+    assert L.brc_cast_block_fp8(p, 0, 4, 100, 128, 0, p, p, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_cast_mxfp8(p, 0, 4, 48, 0, p, p, None, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_cast_block_fp8(p, 7, 4, 128, 128, 0, p, p, None) == _lib.BRC_ERR_DTYPE
+    assert L.brc_cast_block_fp8(p, 0, 4, 128, 128, 9, p, p, None) == _lib.BRC_ERR_DTYPE
+    assert L.brc_cast_block_fp8(p + 4, 0, 4, 128, 128, 0, p, p, None) == _lib.BRC_ERR_ALIGN
+    assert L.brc_cast_int4(p, 0, 4, 128, 128, 1, 0, 0, p, None, p, p, None) == \
+        _lib.BRC_ERR_UNSUPPORTED  # asymmetric + signed is not a valid recipe
+    assert L.brc_dequant_nvfp4(p, 4, 24, p, p, 0, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_dequant_mxfp8(p, 4, 64, 0, p, p, 5, None) == _lib.BRC_ERR_DTYPE
+
+
+def test_empty_inputs_are_noops():
+    L = _lib.lib()
+    _, p = _buf()
+    assert L.brc_cast_block_fp8(p, 0, 0, 128, 128, 0, p, p, None) == _lib.BRC_OK
+    assert L.brc_cast_mxfp8(p, 1, 0, 64, 0, p, p, None, None) == _lib.BRC_OK
+    assert L.brc_amax_accumulate(None, 0, 0, p, None) == _lib.BRC_OK
+
+
+def test_call_raises_python_exceptions():
+    _, p = _buf()
+    with pytest.raises(ValueError):
+        _lib.call("brc_cast_block_fp8", p, 0, 4, 100, 128, 0, p, p, None)
+    with pytest.raises(TypeError):
+        _lib.call("brc_cast_block_fp8", p, 5, 4, 128, 128, 0, p, p, None)
+    with pytest.raises(_lib.BrecciaB200Error):
+        _lib.call("brc_cast_block_fp8", None, 0, 4, 128, 128, 0, p, p, None)

@@ -1,0 +1,303 @@
+"""GPU parity of the cast / dequantize / requantize kernels with the
+reference's NumPy path: bit-exact codes, scales and zero points, bit-exact
+dequantized values (NaN positions must match; NaN payloads may differ).
+
+Sources of truth: golden vectors produced by the reference itself
+(tests/golden/), and the CPU oracle (oracle/, pinned to those vectors) for
+random and full-size inputs. Full-size casts are checked on sampled rows:
+every block recipe is row-independent, and the per-tensor recipe is
+elementwise once its scale is known.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, golden_recipes, golden_requant_pairs, golden_cases, same_bits
+
+pytestmark = pytest.mark.gpu
+
+CASTS = load_golden("casts.npz")
+REQ = load_golden("requant.npz")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _needs_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def bb():
+    import breccia_b200
+    return breccia_b200
+
+
+def _np(t):
+    if t is None:
+        return None
+    if t.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+        t = t.view(torch.uint8)
+    if t.dtype == torch.bfloat16:
+        t = t.float()
+    return t.detach().cpu().numpy()
+
+
+def assert_deq_equal(got, want):
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    gn, wn = np.isnan(got), np.isnan(want)
+    assert np.array_equal(gn, wn), "NaN positions differ"
+    assert same_bits(np.where(gn, 0, got), np.where(wn, 0, want))
+
+
+def assert_cast_equal(st, q, check_deq=True):
+    assert same_bits(_np(st.data), q.data), _first_diff(_np(st.data), q.data)
+    s = _np(st.scale)
+    assert s.dtype == q.scale.dtype, (s.dtype, q.scale.dtype)
+    assert same_bits(s, q.scale), _first_diff(s, q.scale)
+    if q.zero_point is None:
+        assert st.zero_point is None
+    else:
+        assert same_bits(_np(st.zero_point), q.zero_point)
+
+
+def _first_diff(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    if a.shape != b.shape:
+        return f"shape {a.shape} vs {b.shape}"
+    u = {1: np.uint8, 2: np.uint16, 4: np.uint32}[a.dtype.itemsize]
+    idx = np.argwhere(a.view(u) != b.view(u))
+    if not len(idx):
+        return "equal"
+    i = tuple(idx[0])
+    return f"{len(idx)} differences; first at {i}: got {a[i]!r} want {b[i]!r}"
+
+
+# ------------------------------------------------------------- golden cases
+
+
+@pytest.mark.parametrize("case", golden_cases(CASTS), ids=lambda c: "__".join(c))
+def test_golden_cast(case):
+    rname, iname = case
+    key = f"{rname}__{iname}"
+    r = golden_recipes()[rname]
+    x = torch.from_numpy(CASTS[key + "__x"]).cuda()
+    st = bb().cast(x, r)
+    assert st.recipe is r
+    assert same_bits(_np(st.data), CASTS[key + "__data"]), \
+        _first_diff(_np(st.data), CASTS[key + "__data"])
+    assert same_bits(_np(st.scale), CASTS[key + "__scale"]), \
+        _first_diff(_np(st.scale), CASTS[key + "__scale"])
+    if key + "__zp" in CASTS:
+        assert same_bits(_np(st.zero_point), CASTS[key + "__zp"])
+    assert_deq_equal(_np(bb().dequantize(st)), CASTS[key + "__deq"])
+
+
+@pytest.mark.parametrize("case", [c for c in golden_cases(CASTS) if c[1] == "gauss_bf16"],
+                         ids=lambda c: "__".join(c))
+def test_golden_cast_bf16_input(case):
+    """bf16 inputs are read directly; their float32 values equal the golden x."""
+    rname, iname = case
+    key = f"{rname}__{iname}"
+    x = torch.from_numpy(CASTS[key + "__x"]).cuda().to(torch.bfloat16)
+    st = bb().cast(x, golden_recipes()[rname])
+    assert same_bits(_np(st.data), CASTS[key + "__data"])
+    assert same_bits(_np(st.scale), CASTS[key + "__scale"])
+
+
+@pytest.mark.parametrize("case", golden_cases(REQ), ids=lambda c: "__".join(c))
+def test_golden_requantize(case):
+    pname, iname = case
+    key = f"{pname}__{iname}"
+    r1, r2 = golden_requant_pairs()[pname]
+    x = torch.from_numpy(REQ[key + "__x"]).cuda()
+    st = bb().requantize(bb().cast(x, r1), r2)
+    assert same_bits(_np(st.data), REQ[key + "__data"]), _first_diff(_np(st.data), REQ[key + "__data"])
+    assert same_bits(_np(st.scale), REQ[key + "__scale"])
+
+
+# ------------------------------------------------------------- random inputs
+
+def _recipes():
+    from breccia_b200.types import (DelayedScaling, Float8CurrentScaling, Float8BlockScaling,
+                                    MXFP8BlockScaling, NVFP4BlockScaling, INT4Scaling)
+    return {
+        "current_e4m3": Float8CurrentScaling(),
+        "delayed_e5m2": DelayedScaling(fp8_format="E5M2"),
+        "block128": Float8BlockScaling(block_k=128),
+        "block64_e5m2": Float8BlockScaling(block_k=64, fp8_format="E5M2"),
+        "block256": Float8BlockScaling(block_k=256),
+        "block16": Float8BlockScaling(block_k=16),
+        "block96_generic": Float8BlockScaling(block_k=96),
+        "mxfp8": MXFP8BlockScaling(),
+        "mxfp8_e5m2": MXFP8BlockScaling(fp8_format="E5M2"),
+        "nvfp4": NVFP4BlockScaling(),
+        "int4_sym": INT4Scaling(group_size=128),
+        "int4_sym_u_g64": INT4Scaling(group_size=64, signed=False, scale_dtype="fp32"),
+        "int4_asym": INT4Scaling(group_size=128, signed=False, symmetric=False),
+        "int4_asym_g32_bf16scale": INT4Scaling(group_size=32, signed=False, symmetric=False,
+                                               scale_dtype="bf16"),
+        "int4_g48_generic": INT4Scaling(group_size=48),
+    }
+
+
+def _random_input(rows, cols, seed, spread=30):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, cols, generator=g)
+    # per-row magnitudes over many binades, some outliers, some exact zeros
+    x *= torch.exp2(torch.randint(-spread, spread, (rows, 1), generator=g).float())
+    mask = torch.rand(rows, cols, generator=g) < 0.002
+    x[mask] *= 300.0
+    x[torch.rand(rows, cols, generator=g) < 0.01] = 0.0
+    return x
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rname", list(_recipes()))
+def test_random_vs_oracle(rname, dtype):
+    from oracle import cast as ocast
+    r = _recipes()[rname]
+    cols = 1152 if "generic" in rname else 1024
+    seed = sum(map(ord, rname))
+    if dtype == torch.float16:
+        x = _random_input(192, cols, seed, spread=6).clamp(-6e4, 6e4)  # float16 range
+    else:
+        x = _random_input(192, cols, seed)
+    xd = x.to(dtype)
+    st = bb().cast(xd.cuda(), r)
+    q = ocast.cast(xd.float().numpy(), r)
+    assert_cast_equal(st, q)
+    assert_deq_equal(_np(bb().dequantize(st)), ocast.dequantize(q))
+
+
+def test_rank3_and_views():
+    from oracle import cast as ocast
+    from breccia_b200.types import MXFP8BlockScaling, Float8BlockScaling
+    x = torch.randn(3, 40, 256)
+    for r in (MXFP8BlockScaling(), Float8BlockScaling(block_k=128)):
+        st = bb().cast(x.cuda(), r)
+        assert tuple(st.scale.shape) == (3, 40, 256 // (32 if r.name == "mxfp8" else 128))
+        assert_cast_equal(st, ocast.cast(x.numpy(), r))
+    # a non-contiguous, offset view is copied to an aligned buffer first
+    big = torch.randn(64, 300).cuda()
+    view = big[3:, 12:268]
+    st = bb().cast(view, MXFP8BlockScaling())
+    assert_cast_equal(st, ocast.cast(view.cpu().numpy(), MXFP8BlockScaling()))
+
+
+def test_empty_and_errors():
+    from breccia_b200.types import (Float8CurrentScaling, Float8BlockScaling, MXFP8BlockScaling,
+                                    INT4Scaling)
+    st = bb().cast(torch.empty(0, 64).cuda(), MXFP8BlockScaling())
+    assert tuple(st.data.shape) == (0, 64) and tuple(st.scale.shape) == (0, 2)
+    st = bb().cast(torch.empty(0).cuda(), Float8CurrentScaling())
+    # tensor_amax of an empty tensor is 0 -> floored to 1e-10 (float64)
+    assert st.scale.item() == np.float32(1e-10 / 448.0)
+    with pytest.raises(ValueError, match="K=100 must be divisible by block_k=128"):
+        bb().cast(torch.zeros(2, 100).cuda(), Float8BlockScaling())
+    with pytest.raises(ValueError, match="last-axis size 48 must be divisible by block_size 32"):
+        bb().cast(torch.zeros(2, 48).cuda(), MXFP8BlockScaling())
+    with pytest.raises(ValueError, match="requires x.ndim >= 2"):
+        bb().cast(torch.zeros(64).cuda(), MXFP8BlockScaling())
+    with pytest.raises(ValueError, match="K=64 must be divisible by group_size=128"):
+        bb().cast(torch.zeros(2, 64).cuda(), INT4Scaling())
+
+
+def test_float64_and_int_inputs_convert_like_numpy():
+    from oracle import cast as ocast
+    from breccia_b200.types import MXFP8BlockScaling
+    x = torch.randn(8, 64, dtype=torch.float64) * 3
+    st = bb().cast(x.cuda(), MXFP8BlockScaling())
+    assert_cast_equal(st, ocast.cast(x.numpy().astype(np.float32), MXFP8BlockScaling()))
+
+
+def test_packed_side_outputs():
+    """Packed nibbles (element 2i low) and tcgen05-layout scales match the
+    unpacked codes / reference-layout scales."""
+    from breccia_b200.types import NVFP4BlockScaling, MXFP8BlockScaling
+    x = torch.randn(256, 512).cuda()
+    st = bb().cast(x, NVFP4BlockScaling())
+    side = bb().gemm_operands(st)
+    codes = st.data.cpu().numpy()
+    packed = side["packed"].cpu().numpy()
+    np.testing.assert_array_equal(packed & 0xF, codes[:, 0::2])
+    np.testing.assert_array_equal(packed >> 4, codes[:, 1::2])
+    for r, nsf in ((NVFP4BlockScaling(), 512 // 16), (MXFP8BlockScaling(), 512 // 32)):
+        st = bb().cast(x, r)
+        sf = st.scale.cpu().numpy()
+        mma = bb().gemm_operands(st)["sf_mma"].cpu().numpy()
+        rows = np.arange(256)[:, None]
+        cols = np.arange(nsf)[None, :]
+        off = ((rows // 128) * ((nsf + 3) // 4) + cols // 4) * 512 + (rows % 32) * 16 + \
+            ((rows // 32) % 4) * 4 + cols % 4
+        np.testing.assert_array_equal(mma[off], sf)
+
+
+def test_division_matches_ieee():
+    from breccia_b200 import _lib
+    g = torch.Generator().manual_seed(5)
+    n = 1 << 24
+    # quotients across 2^-40..2^40 with random scales over many binades
+    x = torch.exp2(torch.empty(n).uniform_(-60, 60, generator=g)) * torch.sign(torch.randn(n, generator=g))
+    s = torch.exp2(torch.empty(n).uniform_(-40, 40, generator=g))
+    x, s = x.cuda(), s.cuda()
+    qf, qi = torch.empty_like(x), torch.empty_like(x)
+    _lib.call("brc_selftest_division", x.data_ptr(), s.data_ptr(), n, qf.data_ptr(),
+              qi.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert torch.equal(qf.view(torch.int32), qi.view(torch.int32))
+    assert torch.equal(qi, x / s)
+
+
+# ------------------------------------------------------------- full sizes
+
+
+def _sample_rows(n, k, seed=0):
+    g = np.random.default_rng(seed)
+    return np.sort(g.choice(n, size=min(k, n), replace=False))
+
+
+def _config_inputs(name):
+    """BASELINE.json configs, generated as seeded torch tensors on the CPU."""
+    g = torch.Generator().manual_seed(0)
+    if name == "c1_A":
+        return torch.randn(2048, 7168, generator=g)
+    if name == "c2_A":
+        a = torch.randn(16384, 8192, generator=g)
+        m = torch.rand(16384, 8192, generator=g) < 0.001
+        a[m] = torch.randn(int(m.sum()), generator=g) * 50
+        return a.to(torch.bfloat16)
+    if name == "c3_A":
+        return torch.randn(8192, 8192, generator=g).to(torch.bfloat16)
+    if name == "c4_Wt":
+        w = torch.distributions.StudentT(4.0).sample((28672, 8192)) * 0.02
+        return w.to(torch.bfloat16)
+    if name == "c5_Wt":
+        return torch.randn(28672, 8192, generator=g) * 0.02
+    raise KeyError(name)
+
+
+@pytest.mark.parametrize("cfg,rname", [
+    ("c1_A", "block128"), ("c2_A", "current_e4m3"), ("c3_A", "mxfp8"),
+    ("c4_Wt", "nvfp4"), ("c5_Wt", "int4_asym"),
+])
+def test_full_size_sampled_rows(cfg, rname):
+    from oracle import cast as ocast, codec
+    r = _recipes()[rname]
+    x = _config_inputs(cfg)
+    xd = x.cuda()
+    st = bb().cast(xd, r)
+    rows = _sample_rows(x.shape[0], 48)
+    xs = x[rows].float().numpy()
+    data = _np(st.data[rows])
+    if rname == "current_e4m3":
+        amax = float(x.float().abs().max())
+        scale = np.float32(max(amax, 1e-10) / 448.0)
+        assert _np(st.scale) == scale
+        want = codec.encode_e4m3(xs / scale)
+        assert same_bits(data, want), _first_diff(data, want)
+        return
+    q = ocast.cast(xs, r)
+    assert same_bits(data, q.data), _first_diff(data, q.data)
+    assert same_bits(_np(st.scale[rows]), q.scale)
+    if q.zero_point is not None:
+        assert same_bits(_np(st.zero_point[rows]), q.zero_point)

@@ -1,0 +1,167 @@
+"""GPU parity of the tcgen05 scaled GEMMs with the reference's matmul
+(dequantize both operands, float32 matmul: src/breccia/kernels/reference/
+matmul.py:123-133).
+
+Tolerance: max |gpu - ref| / max |ref| <= 1e-2 and
+cosine similarity >= 0.9999. The operands are exactly representable, so the
+only differences are float32 summation order and the output rounding; the
+tests also check the much tighter bound that this implies for float32 output.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-2
+MIN_COS = 0.9999
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _needs_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def bb():
+    import breccia_b200
+    return breccia_b200
+
+
+def _metrics(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rel = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+    cos = float((got.ravel() @ ref.ravel()) /
+                (np.linalg.norm(got) * np.linalg.norm(ref) + 1e-300))
+    return rel, cos
+
+
+def _check(got, ref, tight=None):
+    rel, cos = _metrics(got, ref)
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
+    if tight is not None:
+        assert rel <= tight, rel
+
+
+def _recipe(kind):
+    from breccia_b200.types import (Float8CurrentScaling, DelayedScaling, MXFP8BlockScaling,
+                                    NVFP4BlockScaling)
+    return {"current": Float8CurrentScaling(), "delayed_e5m2": DelayedScaling(fp8_format="E5M2"),
+            "mxfp8": MXFP8BlockScaling(), "mxfp8_e5m2": MXFP8BlockScaling(fp8_format="E5M2"),
+            "nvfp4": NVFP4BlockScaling()}[kind]
+
+
+def _gemm_status():
+    from breccia_b200 import _lib
+    return _lib.lib().brc_gemm_status(1)
+
+
+def _operands(M, N, K, seed, heavy=False):
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    if heavy:
+        W = (torch.distributions.StudentT(4.0).sample((N, K)) * 0.02).to(torch.bfloat16)
+    else:
+        W = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    return A, W
+
+
+@pytest.mark.parametrize("kind", ["current", "mxfp8", "nvfp4"])
+def test_single_tile(kind):
+    """Smallest case: one 128 x 256 tile, one or two K stages."""
+    from oracle import cast as ocast
+    r = _recipe(kind)
+    K = 256
+    A, W = _operands(128, 256, K, seed=1)
+    sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
+    out = bb().linear(sa, sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _gemm_status() == 0
+    qa, qw = ocast.cast(A.float().numpy(), r), ocast.cast(W.float().numpy(), r)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-5)
+
+
+@pytest.mark.parametrize("kind", ["current", "delayed_e5m2", "mxfp8", "mxfp8_e5m2", "nvfp4"])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (200, 384, 512), (1, 256, 512),
+                                   (384, 1040, 768)])
+def test_linear_vs_oracle(kind, M, N, K):
+    from oracle import cast as ocast
+    if kind == "nvfp4" and K % 256:
+        pytest.skip("NVFP4 GEMM needs K % 256 == 0")
+    r = _recipe(kind)
+    A, W = _operands(M, N, K, seed=M + N + K, heavy=(kind == "nvfp4"))
+    sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
+    out = bb().linear(sa, sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _gemm_status() == 0
+    qa, qw = ocast.cast(A.float().numpy(), r), ocast.cast(W.float().numpy(), r)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-5)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("kind", ["current", "mxfp8", "nvfp4"])
+def test_output_dtypes(kind, out_dtype):
+    from oracle import cast as ocast
+    r = _recipe(kind)
+    A, W = _operands(256, 512, 512, seed=3)
+    out = bb().linear(bb().cast(A.cuda(), r), bb().cast(W.cuda(), r), out_dtype=out_dtype)
+    assert out.dtype == out_dtype
+    qa, qw = ocast.cast(A.float().numpy(), r), ocast.cast(W.float().numpy(), r)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    _check(out.float().cpu().numpy(), ref)
+
+
+def test_tensor_core_path_is_taken():
+    """The fast path must not silently fall back to the float32 reference
+    semantics for the supported recipe pairs."""
+    from breccia_b200 import gemm
+    A, W = _operands(128, 256, 256, seed=4)
+    for kind in ("current", "mxfp8", "nvfp4"):
+        r = _recipe(kind)
+        sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
+        assert gemm._tc_pair(sa, sw) is not None, kind
+
+
+def test_golden_matmul_kmajor():
+    """Reference matmul outputs (tests/golden/matmul.npz, K-major weight)."""
+    MM = load_golden("matmul.npz")
+    A, W = MM["A"], MM["W"]  # (64, 512), (512, 256)
+    for name in ("current", "mxfp8", "nvfp4"):
+        r = _recipe(name)
+        sa = bb().cast(torch.from_numpy(A).cuda(), r)
+        sw = bb().cast(torch.from_numpy(np.ascontiguousarray(W.T)).cuda(), r)
+        out = bb().linear(sa, sw, out_dtype=torch.float32).cpu().numpy()
+        _check(out, MM[f"{name}__nk"], tight=1e-5)
+
+
+def test_reference_semantics_matmul():
+    """matmul(a, b) with b (K, N) as in the reference; per-tensor goes to the
+    tensor cores, block recipes in the reference layout use float32."""
+    import numpy as np
+    MM = load_golden("matmul.npz")
+    A, W = MM["A"], MM["W"]
+    for name in ("current", "mxfp8", "nvfp4"):
+        r = _recipe(name)
+        sa = bb().cast(torch.from_numpy(A).cuda(), r)
+        sb = bb().cast(torch.from_numpy(W).cuda(), r)
+        out = bb().matmul(sa, sb)
+        assert out.dtype == torch.float32
+        _check(out.cpu().numpy(), MM[f"{name}__kn"], tight=1e-5)
+    out = bb().matmul(bb().cast(torch.from_numpy(A).cuda(), _recipe("current")),
+                      bb().cast(torch.from_numpy(W).cuda(), _recipe("current")),
+                      out_dtype=np.float16)
+    assert out.dtype == torch.float16
+
+
+def test_shape_mismatch_raises():
+    r = _recipe("current")
+    a = bb().cast(torch.randn(4, 128).cuda(), r)
+    b = bb().cast(torch.randn(64, 16).cuda(), r)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        bb().matmul(a, b)
