@@ -1,0 +1,513 @@
+#!/usr/bin/env python
+"""Benchmark of breccia's hot path on B200: cast + scaled GEMM.
+
+Headline workload (Float8CurrentScaling E4M3):
+  A bf16 (16384, 8192) ~ N(0,1) with 0.1% of entries replaced by N(0,1)*50,
+  W bf16 (8192, 8192) ~ N(0,0.02), held as W^T (N, K) (nn.Linear orientation).
+  One step = per-tensor cast of A + per-tensor cast of W^T + the 16384 x 8192 x
+  8192 tcgen05 FP8 GEMM -> bf16.
+  N GPUs: W^T is split along N (rows); the weight's amax is reduced with one
+  NCCL all-reduce(MAX) of 4 bytes; A is replicated; each rank computes its
+  C[:, shard]. Total work is fixed ("strong" scaling).
+
+value = 2*M*N*K / step time (max over ranks), whole job.
+e2e   = the same through the public API with the inputs copied from pinned
+        host memory and the output C copied back inside every step.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Under torchrun one process per GPU; rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, N, K = 16384, 8192, 8192
+FLOPS = 2.0 * M * N * K
+WORKLOAD = ("C2 Float8CurrentScaling E4M3 per-tensor: A bf16 (16384, 8192) N(0,1) with 0.1% "
+            "N(0,1)*50 outliers, W bf16 (8192, 8192) N(0,0.02) held as W^T; cast A + cast W "
+            "+ 16384x8192x8192 tcgen05 FP8 GEMM -> bf16")
+METRIC = "scaled-matmul TFLOP/s (C2 per-tensor FP8: cast A + cast W + GEMM, whole job)"
+
+# DRAM bytes per launch of the GEMM kernel from one ncu capture of this
+# workload (profiles/gemm_fp8_pertensor_c2.txt); None until captured.
+GEMM_DRAM_BYTES = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--per-recipe", action="store_true",
+                    help="also measure every BASELINE config's cast GB/s and GEMM TFLOP/s")
+    ap.add_argument("--cpu-rows", type=int, default=64,
+                    help="rows of A / W^T the CPU baseline encodes per sample")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------- CPU side
+
+
+def _cpu_encode_rows(args):
+    """Worker: the reference's per-tensor encode (literal LUT search) of rows."""
+    x, scale, fmt = args
+    import numpy as np
+    from oracle import codec
+    x = np.asarray(x, dtype=np.float32)
+    enc = codec.encode_e4m3 if fmt == "E4M3" else codec.encode_e5m2
+    t0 = time.perf_counter()
+    enc(x / np.float32(scale), literal=True)
+    return time.perf_counter() - t0
+
+
+def cpu_reference_step(A_np, Wt_np, rows, pool, nproc):
+    """Time the reference NumPy path on a bounded sample of the C2 step and
+    extrapolate to the whole step by rows (the per-tensor encode is elementwise
+    once the scale is known; the matmul is row-separable in A).
+
+    Returns (seconds for the whole step, breakdown dict)."""
+    import numpy as np
+    from oracle import codec, cast as ocast
+
+    t = {}
+    t0 = time.perf_counter()
+    amax_a = codec.tensor_amax(A_np)
+    t["amax_A"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    amax_w = codec.tensor_amax(Wt_np)
+    t["amax_W"] = time.perf_counter() - t0
+    sa = np.float32(amax_a / 448.0)
+    sw = np.float32(amax_w / 448.0)
+    # encode `rows` rows of A and of W^T, split over the pool
+    chunks = [(A_np[i::nproc][: max(1, rows // nproc)], sa, "E4M3") for i in range(nproc)]
+    chunks += [(Wt_np[i::nproc][: max(1, rows // nproc)], sw, "E4M3") for i in range(nproc)]
+    t0 = time.perf_counter()
+    list(pool.map(_cpu_encode_rows, chunks))
+    t_enc = time.perf_counter() - t0  # wall time for ~rows rows of A and of W^T
+    per_row_enc = t_enc / (2 * nproc * max(1, rows // nproc))
+    t["encode_A"] = per_row_enc * A_np.shape[0]
+    t["encode_W"] = per_row_enc * Wt_np.shape[0]
+    # reference matmul: dequantize both (LUT decode * scale), float32 sgemm
+    qa = codec.encode_e4m3(A_np[:rows] / sa)
+    qw_rows = codec.encode_e4m3(Wt_np[:rows] / sw)
+    t0 = time.perf_counter()
+    da = codec.decode_e4m3(qa) * sa
+    t["dequant_A"] = (time.perf_counter() - t0) * A_np.shape[0] / rows
+    t0 = time.perf_counter()
+    dw = codec.decode_e4m3(qw_rows) * sw
+    t["dequant_W"] = (time.perf_counter() - t0) * Wt_np.shape[0] / rows
+    dW = np.ascontiguousarray(np.broadcast_to(dw[:1], Wt_np.shape)).T  # full-size operand
+    t0 = time.perf_counter()
+    _ = da @ dW
+    t["sgemm"] = (time.perf_counter() - t0) * A_np.shape[0] / rows
+    return sum(t.values()), t
+
+
+def run_reference(args):
+    """--impl reference: the oracle port of breccia's NumPy path on the host."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import multiprocessing as mp
+    import numpy as np
+    from concurrent.futures import ProcessPoolExecutor
+    A_np, Wt_np = host_inputs_numpy()
+    nproc = os.cpu_count() or 1
+    times = []
+    with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as pool:
+        _warm_pool(pool, nproc)
+        for i in range(args.warmup + args.steps):
+            t, _ = cpu_reference_step(A_np, Wt_np, args.cpu_rows, pool, nproc)
+            if i >= args.warmup:
+                times.append(t)
+    sec = statistics.mean(times)
+    value = FLOPS / sec / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (numpy)", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nproc, "kind": "port",
+                         "sample": f"{args.cpu_rows} rows of A and of W^T encoded per step "
+                                   "(literal LUT search, process pool), full-tensor amax, "
+                                   f"{args.cpu_rows}-row dequant + sgemm; extrapolated by rows"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def host_inputs_numpy():
+    """C2 inputs as float32 NumPy arrays (the reference's np.asarray(x, float32)
+    of the bf16 values), generated with the same seeded torch generator."""
+    A, Wt = make_inputs("cpu")
+    return A.float().numpy(), Wt.float().numpy()
+
+
+# --------------------------------------------------------------- GPU side
+
+
+def make_inputs(device):
+    import torch
+    g = torch.Generator(device=device).manual_seed(0)
+    A = torch.randn(M, K, generator=g, device=device)
+    mask = torch.rand(M, K, generator=g, device=device) < 0.001
+    A = torch.where(mask, torch.randn(M, K, generator=g, device=device) * 50, A)
+    A = A.to(torch.bfloat16)
+    W = (torch.randn(K, N, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return A, W.t().contiguous()
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for ln in (self.out or "").splitlines():
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            if self.uuid and parts[0] != self.uuid:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        active = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": active, "samples": len(rows)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, \
+            "fallback"
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import breccia_b200 as bb
+    from breccia_b200.dist import shard_rows, cast_per_tensor_sharded
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    recipe = bb.Float8CurrentScaling(fp8_format="E4M3")
+    A, Wt = make_inputs(dev)
+    n0, n1 = shard_rows(N, world, rank)
+    Wt_sh = Wt[n0:n1].contiguous()
+    del Wt
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    gemm_events = []
+
+    def step(a_in, w_in, record=False):
+        sa = bb.cast(a_in, recipe)
+        sw = cast_per_tensor_sharded(w_in, recipe)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        out = bb.linear(sa, sw, out_dtype=torch.bfloat16)
+        if record:
+            e1.record()
+            gemm_events.append((e0, e1))
+        return out
+
+    # ---- device-resident timing
+    for _ in range(args.warmup):
+        step(A, Wt_sh)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid) \
+        if hasattr(torch.cuda.get_device_properties(dev), "uuid") else None
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with Clocks(uuid) as clk:
+        t_start.record()
+        for _ in range(args.steps):
+            step(A, Wt_sh, record=True)
+        t_end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
+    ms_t = torch.tensor([ms, gemm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, gemm_ms_max = ms_t.tolist()
+    value = FLOPS / (ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API, host buffers
+    e2e = None
+    if not args.no_e2e:
+        A_h = A.cpu().pin_memory()
+        W_h = Wt_sh.cpu().pin_memory()
+        out_h = torch.empty((M, n1 - n0), dtype=torch.bfloat16).pin_memory()
+        A_d = torch.empty_like(A)
+        W_d = torch.empty_like(Wt_sh)
+
+        def e2e_step():
+            A_d.copy_(A_h, non_blocking=True)
+            W_d.copy_(W_h, non_blocking=True)
+            out = step(A_d, W_d)
+            out_h.copy_(out, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": FLOPS / (e_ms.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": A_h.numel() * 2 + W_h.numel() * 2,
+               "d2h_bytes_per_step": out_h.numel() * 2,
+               "ms_per_step": e_ms.item()}
+        if world > 1:
+            hb = torch.tensor([e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]],
+                              device=dev, dtype=torch.float64)
+            dist.all_reduce(hb)
+            e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"] = [int(v) for v in hb.tolist()]
+
+    # ---- roofline of the dominant kernel (the GEMM), per rank
+    peaks, src = measured_peaks()
+    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    gemm_flops_rank = 2.0 * M * (n1 - n0) * K
+    achieved = gemm_flops_rank / (gemm_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_fp8, "unit": "TFLOP/s",
+                "frac": achieved / peak_fp8, "traffic": GEMM_DRAM_BYTES,
+                "kernel": "brc::gemm::k_gemm<kPerTensor,E4M3,E4M3,bf16>",
+                "peak_source": f"2 x bf16_tflops_sustained of {src} MEASURED_PEAKS.json "
+                               "(dense FP8 = 2x dense bf16)",
+                "frac_vs_burst": achieved / (2.0 * peaks["bf16_tflops"]),
+                "gemm_ms": gemm_ms}
+
+    extras = {}
+    if args.per_recipe and world == 1:
+        del A, Wt_sh
+        torch.cuda.empty_cache()
+        extras = per_recipe(peaks, src)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> f32 accumulate -> bf16 out",
+            "data": "synthetic (seeded torch generator, BASELINE configs[1] shapes/distributions)",
+            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K,
+                       "parallelism": "single GPU" if world == 1 else
+                       f"W^T split along N over {world} GPUs, A replicated, "
+                       "one NCCL all-reduce(MAX) of the weight amax",
+                       "l2": "inputs larger than L2 (A is 268 MB)"},
+            "clocks": clk.summary(),
+            "e2e": e2e,
+            "gpu_launches": 7 * args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+        }
+        if extras:
+            line["per_recipe"] = extras
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def _warm_pool(pool, nproc):
+    import numpy as np
+    list(pool.map(_cpu_encode_rows, [(np.zeros((1, 16), np.float32), 1.0, "E4M3")] * nproc))
+
+
+def cpu_baseline(args):
+    """Rank 0, N = 1: the oracle port of the reference, bounded sample."""
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
+    A_np, Wt_np = host_inputs_numpy()
+    nproc = os.cpu_count() or 1
+    with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as pool:
+        _warm_pool(pool, nproc)
+        sec, parts = cpu_reference_step(A_np, Wt_np, args.cpu_rows, pool, nproc)
+    return {"value": FLOPS / sec / 1e12, "unit": "TFLOP/s", "cores": nproc, "kind": "port",
+            "sample": f"{args.cpu_rows} rows of A and of W^T encoded (literal LUT search, "
+                      f"{nproc} spawn processes), full-tensor amax, {args.cpu_rows}-row dequant "
+                      "+ sgemm; extrapolated linearly by rows",
+            "seconds_per_step": sec,
+            "breakdown_s": {k: round(v, 3) for k, v in parts.items()}}
+
+
+# --------------------------------------------------------------- per recipe
+
+
+def _time_ms(fn, iters=10, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def per_recipe(peaks, src):
+    """Every BASELINE config at full size on one GPU: cast GB/s (algorithmic
+    bytes: input read once -- twice for per-tensor, whose global amax must be
+    known before any code is written -- plus codes, scales and side outputs
+    written) and GEMM TFLOP/s. Inputs exceed L2 except where noted."""
+    import torch
+    import breccia_b200 as bb
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(1)
+    hbm = peaks["hbm_gbs"]
+    fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    fp4 = 4.0 * peaks["bf16_tflops_sustained"]
+    res = {}
+
+    def cast_entry(name, x, r, bytes_, **kw):
+        ms = _time_ms(lambda: bb.cast(x, r, **kw))
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm}
+
+    def gemm_entry(name, a, w, m, n, k, peak):
+        ms = _time_ms(lambda: bb.linear(a, w, out_dtype=torch.bfloat16))
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        res[name] = {"ms": ms, "TFLOP/s": tf, "frac_peak": tf / peak}
+
+    # C1 Float8BlockScaling: A f32 (2048, 7168) 1x128; W^T f32 (4096, 7168) 128x128
+    A = torch.randn(2048, 7168, generator=g, device=dev)
+    Wt = torch.randn(4096, 7168, generator=g, device=dev) * 0.02
+    r = bb.Float8BlockScaling(block_k=128)
+    cast_entry("c1_cast_A_block1x128_f32", A, r, A.numel() * 5 + A.numel() // 128 * 4)
+    cast_entry("c1_cast_Wt_block128x128_f32", Wt, r, Wt.numel() * 5 + Wt.numel() // 16384 * 4,
+               block_m=128)
+    del A, Wt
+    # C2 per-tensor: A bf16 (16384, 8192): two reads + one write
+    A = torch.randn(16384, 8192, generator=g, device=dev).to(torch.bfloat16)
+    cast_entry("c2_cast_A_pertensor_bf16", A, bb.Float8CurrentScaling(), A.numel() * 5)
+    del A
+    # C3 MXFP8: A bf16 (8192, 8192), W^T bf16 (28672, 8192); GEMM 8192 x 28672 x 8192
+    r = bb.MXFP8BlockScaling()
+    A = torch.randn(8192, 8192, generator=g, device=dev).to(torch.bfloat16)
+    Wt = (torch.randn(28672, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    cast_entry("c3_cast_A_mxfp8_bf16", A, r, A.numel() * 3 + A.numel() // 32 * 2)
+    cast_entry("c3_cast_Wt_mxfp8_bf16", Wt, r, Wt.numel() * 3 + Wt.numel() // 32 * 2)
+    gemm_entry("c3_gemm_mxfp8", bb.cast(A, r), bb.cast(Wt, r), 8192, 28672, 8192, fp8)
+    del A, Wt
+    # C4 NVFP4: A bf16 (4096, 8192), W^T bf16 (28672, 8192) Student-t(4) * 0.02
+    r = bb.NVFP4BlockScaling()
+    A = torch.randn(4096, 8192, generator=g, device=dev).to(torch.bfloat16)
+    Wt = (torch.distributions.StudentT(torch.tensor(4.0, device=dev)).sample((28672, 8192))
+          * 0.02).to(torch.bfloat16)
+    cast_entry("c4_cast_A_nvfp4_bf16", A, r, A.numel() * 3.5 + A.numel() // 16 * 2)
+    cast_entry("c4_cast_Wt_nvfp4_bf16", Wt, r, Wt.numel() * 3.5 + Wt.numel() // 16 * 2)
+    sw = bb.cast(Wt, r)
+    gemm_entry("c4_gemm_nvfp4", bb.cast(A, r), sw, 4096, 28672, 8192, fp4)
+    ms = _time_ms(lambda: bb.requantize(sw, bb.MXFP8BlockScaling()))
+    n = Wt.numel()
+    b = n * 1 + n // 16 + n * 1 + n // 32 * 2
+    res["c4_requant_Wt_nvfp4_to_mxfp8"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
+                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
+    del A, Wt, sw
+    # C5 INT4 asymmetric g128: W^T f32 (28672, 8192)
+    Wt = torch.randn(28672, 8192, generator=g, device=dev) * 0.02
+    r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
+    cast_entry("c5_cast_Wt_int4_asym_f32", Wt, r,
+               Wt.numel() * 5.5 + Wt.numel() // 128 * 4)
+    del Wt
+    torch.cuda.empty_cache()
+    res["peaks"] = {"hbm_gbs": hbm, "fp8_tflops": fp8, "fp4_tflops": fp4,
+                    "source": f"{src} MEASURED_PEAKS.json: hbm_gbs; 2x / 4x "
+                              "bf16_tflops_sustained for dense FP8 / FP4"}
+    return res
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
