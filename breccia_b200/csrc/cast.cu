@@ -1112,3 +1112,138 @@ int brc_requant_nvfp4_to_mxfp8(const uint8_t* codes, const uint8_t* scales, int6
 }
 
 }  // extern "C"
+
+// ========================================================================
+// Per-tensor FP8 cast for callers that cannot allocate device memory.
+//
+// Some callers have no allocator to hand: a host runtime that only receives
+// pre-allocated input and output buffers, a custom-op slot with no workspace
+// argument, or code running where cudaMalloc is not allowed (it would block
+// or break an enclosing memory pool's accounting). brc_cast_pertensor_fp8
+// needs a caller-provided workspace word for the global amax; this variant
+// keeps that scratch in a fixed device array inside the library instead.
+//
+// Scratch: kNoAllocMaxChunks partial maxima (one per kNoAllocChunk-element
+// chunk of the input) plus one final amax word, 65,792 bytes, in a
+// file-scope __device__ array that every GPU loading the library holds until
+// exit. Each call writes every slot it later reads (the chunk partials, then
+// the final word), so nothing has to be cleared between calls. All calls on a
+// device share the array: calls whose kernels overlap on that GPU (different
+// streams, or different host threads) race and must be serialised by the
+// caller.
+// ========================================================================
+namespace brc {
+namespace noalloc {
+
+constexpr int64_t kChunk = 32768;
+constexpr int64_t kMaxChunks = 16384;
+constexpr int64_t kMaxElems = kChunk * kMaxChunks;  // 536,870,912 elements
+constexpr int64_t kFinal = kMaxChunks;              // index of the final amax word
+
+static __device__ __align__(256) uint32_t g_scratch[kMaxChunks + 64];
+
+// One CTA per chunk: abs-max of elements [chunk * kChunk, min(n, ...)).
+template <int DT>
+__global__ void __launch_bounds__(256) k_chunk_amax(const void* __restrict__ x, int64_t n,
+                                                     uint32_t* partials) {
+  constexpr int V = In<DT>::kVec;
+  const int64_t lo = (int64_t)blockIdx.x * kChunk;
+  const int64_t hi = lo + kChunk < n ? lo + kChunk : n;
+  float m = 0.f;
+  if (((hi - lo) % V) == 0) {
+    const char* base = static_cast<const char*>(x) + lo * elem_bytes<DT>();
+    for (int64_t v = threadIdx.x; v < (hi - lo) / V; v += blockDim.x)
+      m = fmax_nan(m, vec_absmax<DT>(ldg16(base + 16 * v)));
+  } else {
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+      m = fmax_nan(m, fabsf(load1<DT>(x, i)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = fmax_nan(t, red[w]);
+    partials[blockIdx.x] = __float_as_uint(t);
+  }
+}
+
+// One CTA: final = max(partials[0..count)), 0 when count == 0.
+__global__ void __launch_bounds__(1024) k_reduce_partials(const uint32_t* partials, int count,
+                                                          uint32_t* final_word) {
+  uint32_t m = 0u;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) m = max(m, partials[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  __shared__ uint32_t red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
+    *final_word = max(m, red[0]);
+  }
+}
+
+}  // namespace noalloc
+}  // namespace brc
+
+#include <mutex>
+
+namespace {
+// Device address of the scratch array, looked up once per device with that
+// device current. In host code `g_scratch` names a host-side shadow, not the
+// device array, so kernels must be given this address.
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+int noalloc_scratch(uint32_t** out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev));
+  if (rc) return rc;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return BRC_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    uint32_t* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), brc::noalloc::g_scratch));
+    if (rc) return rc;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return BRC_OK;
+}
+
+template <int DT, int FMT>
+struct NoAllocCast {
+  static int run(const void* x, int64_t n, uint8_t* codes, float* scale_out, uint32_t* scratch,
+                 cudaStream_t st) {
+    using namespace brc::noalloc;
+    const int chunks = (int)((n + kChunk - 1) / kChunk);
+    if (chunks > 0) {
+      k_chunk_amax<DT><<<chunks, 256, 0, st>>>(x, n, scratch);
+      int rc = check_launch();
+      if (rc) return rc;
+    }
+    k_reduce_partials<<<1, 1024, 0, st>>>(scratch, chunks, scratch + kFinal);
+    int rc = check_launch();
+    if (rc) return rc;
+    return PerTensorApply<DT, FMT>::run(x, n, scratch + kFinal, codes, scale_out, st);
+  }
+};
+}  // namespace
+
+extern "C" int brc_cast_pertensor_fp8_noalloc(const void* x, int x_dtype, int64_t n, int fmt,
+                                              uint8_t* codes, float* scale_out, void* stream) {
+  if (!scale_out || ((!x || !codes) && n > 0)) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype) || !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (n < 0) return BRC_ERR_SHAPE;
+  if (n > brc::noalloc::kMaxElems) return BRC_ERR_RANGE;
+  if (n > 0 && (!aligned16(x) || !aligned16(codes))) return BRC_ERR_ALIGN;
+  uint32_t* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return dispatch_dt_fmt<NoAllocCast>(x_dtype, fmt, x, n, codes, scale_out, scratch,
+                                      (cudaStream_t)stream);
+}

@@ -78,6 +78,22 @@ int brc_cast_pertensor_fp8_apply(const void* x, int x_dtype, int64_t n, int fmt,
 int brc_cast_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt, uint8_t* codes,
                            float* scale_out, uint32_t* workspace, void* stream);
 
+/* Per-tensor FP8 cast that allocates nothing and takes no workspace, for
+ * callers that cannot allocate device memory (a host runtime that hands over
+ * only its input and output buffers, an op slot with no workspace argument,
+ * code running where cudaMalloc is not allowed). No counterpart in the
+ * reference; results equal brc_cast_pertensor_fp8 bit for bit.
+ * The global amax goes through a scratch array inside the library
+ * (16384 partial maxima + one word, 65,792 bytes per GPU that loads the
+ * library, held until exit), so n is limited to 536,870,912 elements
+ * (16384 chunks of 32768); larger inputs return BRC_ERR_RANGE. The first call
+ * on a device looks up the scratch address on the current device; make that
+ * first call before any stream capture. All calls on a device share the
+ * scratch: calls whose kernels overlap on the GPU race and must be
+ * serialised by the caller. Each call rewrites every scratch slot it reads. */
+int brc_cast_pertensor_fp8_noalloc(const void* x, int x_dtype, int64_t n, int fmt,
+                                   uint8_t* codes, float* scale_out, void* stream);
+
 /* ======================================================= casts: block FP8
  * Float8BlockScaling: one float32 scale per `block_k` run of the last axis.
  * Reference: src/breccia/kernels/reference/cast.py:384-404 (_cast_block_fp8),
