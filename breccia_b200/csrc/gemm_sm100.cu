@@ -75,7 +75,8 @@ struct Smem {
   static constexpr uint32_t kSfA = kB + STAGES * B_BYTES;
   static constexpr uint32_t kSfB = kSfA + STAGES * SfCfg<KIND>::A_SF;
   static constexpr uint32_t kBar = kSfB + STAGES * SfCfg<KIND>::B_SF;
-  static constexpr uint32_t kMisc = kBar + 8 * (2 * STAGES + 3);
+  static constexpr uint32_t kNumBars = 2 * STAGES + 8;  // stage ring + accumulator/partial/drain
+  static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
 };
@@ -92,6 +93,10 @@ struct Params {
   void* d;
   int64_t ldd;
   uint32_t* status;
+  // block FP8 (per-K-block promotion): float32 scales
+  const float* bsa;       // (M, K/128): one scale per row per 128-K block
+  const float* bsb;       // (ceil(N/128), K/128): one scale per 128x128 tile of B
+  int bs_ld;              // K / 128
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
@@ -150,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_full = empty + STAGES;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* drain = tmem_empty + 1;
+  static_assert(2 * STAGES + 3 <= L::kNumBars, "barrier area too small");
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
 
@@ -345,6 +351,190 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ block FP8
+// DeepSeek-v3 style Float8BlockScaling: A with 1 x 128 float32 scales, B with
+// 128 x 128 float32 scales. Float32 (non power of two) scales cannot ride in
+// the MMA, so each 128-K block is multiplied into its own TMEM partial (two
+// partial buffers of 256 columns) and the epilogue warps promote it into
+// float32 register accumulators: acc += P_kb * (sa[m, kb] * sb[n / 128, kb]).
+// Each epilogue warp owns one 128-column half of the tile, so its B scale is
+// one value per K block.
+constexpr uint32_t kPartialCols = 256;
+
+template <int AFMT, int BFMT, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_block(const __grid_constant__ CUtensorMap tmap_a,
+                 const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  using L = Smem<kPerTensor>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* pfull = empty + STAGES;   // 2 partial buffers
+  uint64_t* pempty = pfull + 2;
+  uint64_t* drain = pempty + 2;
+  static_assert(2 * STAGES + 5 <= L::kNumBars, "barrier area too small");
+  uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(smem + L::kA + stage * A_BYTES, &tmap_a, kb * BKB, mb * BM, &full[stage]);
+          tma_load_2d(smem + L::kB + stage * B_BYTES, &tmap_b, kb * BKB, nb * BN, &full[stage]);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0, pbuf = 0;
+      uint32_t phase = 0, pphase = 0;
+      bool ok = true;
+      const uint32_t idesc = idesc_f8f6f4(AFMT, BFMT, BM, BN);
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&pempty[pbuf], pphase ^ 1u, abort_flag, p.status, 1u) ||
+              !mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(smem + L::kB + stage * B_BYTES);
+          const uint32_t d = tmem + pbuf * kPartialCols;
+#pragma unroll
+          for (uint32_t k = 0; k < 4; ++k)
+            mma_f8f6f4(d, desc_kmajor_sw128(a_addr + 32 * k), desc_kmajor_sw128(b_addr + 32 * k),
+                       idesc, k > 0 ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          tc_commit(&pfull[pbuf]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          pbuf ^= 1;
+          if (pbuf == 0) pphase ^= 1u;
+        }
+      }
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int half = ew / 4;
+    int pbuf = 0;
+    uint32_t pphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int row = mb * BM + 32 * quad + lane;
+      const int rs = row < p.M ? row : p.M - 1;  // clamp scale reads for rows past M
+      const int bgrp = min(2 * nb + half, (p.N - 1) / 128);
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const float s = __fmul_rn(p.bsa[(int64_t)rs * p.bs_ld + kb],
+                                  p.bsb[(int64_t)bgrp * p.bs_ld + kb]);
+        if (!mbar_wait(&pfull[pbuf], pphase, abort_flag, p.status, 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + pbuf * kPartialCols + 128 * half;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[32 * c + i] = __fmaf_rn(__uint_as_float(r[i]), s, acc[32 * c + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[pbuf]);
+        pbuf ^= 1;
+        if (pbuf == 0) pphase ^= 1u;
+      }
+      if (!ok) break;
+      if (row < p.M) {
+        const int col0 = nb * BN + 128 * half;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          store_row_chunk<OUT>(p.d, p.ldd, row, col0 + 32 * c, p.N, acc + 32 * c, 32);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -406,6 +596,33 @@ int launch_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb, cons
   if (out_dtype == BRC_DTYPE_F32) return launch<KIND, AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, p, st);
   if (out_dtype == BRC_DTYPE_BF16) return launch<KIND, AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, p, st);
   return launch<KIND, AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, p, st);
+}
+
+template <int AFMT, int BFMT, int OUT>
+int launch_block(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  auto kern = k_gemm_block<AFMT, BFMT, OUT>;
+  const int smem = (int)Smem<kPerTensor>::kAlloc;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return BRC_ERR_CUDA;
+  if (!configured[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (rc) return rc;
+    configured[dev] = true;
+  }
+  const int tiles = p.num_m * p.num_n;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return check_launch();
+}
+
+template <int AFMT, int BFMT>
+int launch_block_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const Params& p, cudaStream_t st) {
+  if (out_dtype == BRC_DTYPE_F32) return launch_block<AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, p, st);
+  if (out_dtype == BRC_DTYPE_BF16) return launch_block<AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, p, st);
+  return launch_block<AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, p, st);
 }
 
 int check_common(const void* a, const void* b, void* d, int M, int N, int K, int out_dtype,
@@ -528,6 +745,33 @@ int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int 
   p.sfb_row_atoms = (N + 127) / 128;
   p.status = status_word();
   return launch_out<kNvfp4, 0, 0>(d_dtype, ta, tb, p, (cudaStream_t)stream);
+}
+
+int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                       int b_fmt, const float* a_scales, const float* b_scales, void* d,
+                       int d_dtype, void* stream) {
+  int rc = check_common(a, b, d, M, N, K, d_dtype, BKB);
+  if (rc) return rc;
+  if (!a_scales || !b_scales) return BRC_ERR_NULL;
+  if ((a_fmt != BRC_FP8_E4M3 && a_fmt != BRC_FP8_E5M2) ||
+      (b_fmt != BRC_FP8_E4M3 && b_fmt != BRC_FP8_E5M2))
+    return BRC_ERR_DTYPE;
+  if ((int64_t)M * N == 0) return BRC_OK;
+  if (K == 0) return BRC_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
+  if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
+  Params p = base_params(M, N, K, BKB, d);
+  p.bsa = a_scales;
+  p.bsb = b_scales;
+  p.bs_ld = K / 128;
+  p.status = status_word();
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+    return launch_block_out<0, 0>(d_dtype, ta, tb, p, st);
+  if (a_fmt == BRC_FP8_E4M3) return launch_block_out<0, 1>(d_dtype, ta, tb, p, st);
+  if (b_fmt == BRC_FP8_E4M3) return launch_block_out<1, 0>(d_dtype, ta, tb, p, st);
+  return launch_block_out<1, 1>(d_dtype, ta, tb, p, st);
 }
 
 int brc_gemm_status(int reset) {

@@ -14,6 +14,8 @@ Tensor-core paths (both operands K-major, i.e. ``linear(a, w)`` with ``w`` an
   so a ``(K, N)`` operand is transposed as plain bytes)
 * MXFP8 x MXFP8 -> ``brc_gemm_mxfp8``
 * NVFP4 x NVFP4 -> ``brc_gemm_nvfp4``
+* Float8BlockScaling 1 x 128 activations x 128 x 128 weights (DeepSeek-v3
+  layout, ``cast(w, Float8BlockScaling(), block_m=128)``) -> ``brc_gemm_block_fp8``
 """
 
 from __future__ import annotations
@@ -66,6 +68,12 @@ def _tc_pair(a, w):
     if na == "mxfp8" and nw == "mxfp8" and K % 128 == 0:
         if "sf_mma" in _side(a.data) and "sf_mma" in _side(w.data):
             return "mxfp8"
+    if na == "block" and nw == "block" and K % 128 == 0 and \
+            a.recipe.block_k == 128 and w.recipe.block_k == 128:
+        la, lw = getattr(a.layout, "name", ""), getattr(w.layout, "name", "")
+        if la == "per_block_k" and lw == "per_block_mn" and w.layout.block_m == 128 and \
+                w.layout.block_n == 128:
+            return "block"
     if na == "nvfp4" and nw == "nvfp4" and K % 256 == 0:
         sa, sw = _side(a.data), _side(w.data)
         if "sf_mma" in sa and "packed" in sa and "sf_mma" in sw and "packed" in sw:
@@ -89,6 +97,11 @@ def _run_tc(kind, a, w, out_dtype, w_codes=None):
                       _FMT[a.recipe.fp8_format], _FMT[w.recipe.fp8_format],
                       a.scale.to(torch.float32).data_ptr(), w.scale.to(torch.float32).data_ptr(),
                       out.data_ptr(), _OUT_DT[cdt], st)
+        elif kind == "block":
+            _lib.call("brc_gemm_block_fp8", _codes_u8(a.data).data_ptr(),
+                      _codes_u8(w.data).data_ptr(), M, N, K, _FMT[a.recipe.fp8_format],
+                      _FMT[w.recipe.fp8_format], a.scale.contiguous().data_ptr(),
+                      w.scale.contiguous().data_ptr(), out.data_ptr(), _OUT_DT[cdt], st)
         elif kind == "mxfp8":
             sa, sw = _side(a.data), _side(w.data)
             _lib.call("brc_gemm_mxfp8", _codes_u8(a.data).data_ptr(), _codes_u8(w.data).data_ptr(),

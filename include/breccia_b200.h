@@ -205,6 +205,16 @@ int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int 
 int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int N, int K,
                    const uint8_t* a_sf_mma, const uint8_t* b_sf_mma, void* d, int d_dtype,
                    void* stream);
+/* Float8BlockScaling (DeepSeek-v3 layout): A codes with float32 scales
+ * a_scales (M, K/128) (1 x 128 blocks), B codes with float32 scales
+ * b_scales (ceil(N/128), K/128) (128 x 128 blocks of the (N, K) weight).
+ * Each 128-K block is multiplied on the tensor cores and promoted into float32
+ * accumulators with its two scales. K % 128 == 0.
+ * Reference: matmul.py:42-133 on ScaledTensors from cast.py:384-404;
+ * triton/scaled_matmul.py:263-407 (block_scaled_matmul_triton). */
+int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
+                       int b_fmt, const float* a_scales, const float* b_scales, void* d,
+                       int d_dtype, void* stream);
 /* Sticky device status of the GEMM kernels on the current device (bit 0: a
  * bounded wait timed out and the kernel returned early). Synchronous. */
 int brc_gemm_status(int reset);

@@ -128,6 +128,32 @@ def test_tensor_core_path_is_taken():
         assert gemm._tc_pair(sa, sw) is not None, kind
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (256, 512, 1024), (200, 384, 768),
+                                   (2048, 4096, 7168)])
+@pytest.mark.parametrize("fmt", ["E4M3", "E5M2"])
+def test_block_fp8_deepseek(M, N, K, fmt):
+    """Float8BlockScaling: 1 x 128 activation scales, 128 x 128 weight scales
+    (restated oracle for the weight layout; the reference cannot produce it)."""
+    from oracle import cast as ocast
+    from breccia_b200 import gemm
+    from breccia_b200.types import Float8BlockScaling
+    r = Float8BlockScaling(block_k=128, fp8_format=fmt)
+    g = torch.Generator().manual_seed(M + K)
+    A = torch.randn(M, K, generator=g)
+    Wt = torch.randn(N, K, generator=g) * 0.02
+    Wt[: min(N, 128), :128] *= 40.0  # one tile with a very different scale
+    sa = bb().cast(A.cuda(), r)
+    sw = bb().cast(Wt.cuda(), r, block_m=128)
+    assert gemm._tc_pair(sa, sw) == "block"
+    out = bb().linear(sa, sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _gemm_status() == 0
+    qa = ocast.cast(A.numpy(), r)
+    qw = ocast.cast_block_fp8_2d(Wt.numpy(), r, block_m=128)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-5)
+
+
 def test_golden_matmul_kmajor():
     """Reference matmul outputs (tests/golden/matmul.npz, K-major weight)."""
     MM = load_golden("matmul.npz")
