@@ -56,6 +56,8 @@ def parse():
                     help="also measure every BASELINE config's cast GB/s and GEMM TFLOP/s")
     ap.add_argument("--cpu-rows", type=int, default=64,
                     help="rows of A / W^T the CPU baseline encodes per sample")
+    ap.add_argument("--ncu-case", default=None, choices=sorted(NCU_CASES),
+                    help="run one kernel on a small case (inputs > L2, < 1 GB) 3 times, for ncu")
     return ap.parse_args()
 
 
@@ -461,6 +463,12 @@ def per_recipe(peaks, src):
     cast_entry("c1_cast_A_block1x128_f32", A, r, A.numel() * 5 + A.numel() // 128 * 4)
     cast_entry("c1_cast_Wt_block128x128_f32", Wt, r, Wt.numel() * 5 + Wt.numel() // 16384 * 4,
                block_m=128)
+    ms = _time_ms(lambda: bb.linear(bb.cast(A, r), bb.cast(Wt, r, block_m=128),
+                                    out_dtype=torch.float32))
+    res["c1_step_cast_both_gemm_block_fp8_f32out"] = {
+        "ms": ms, "TFLOP/s": 2.0 * 2048 * 4096 * 7168 / (ms * 1e-3) / 1e12}
+    gemm_entry("c1_gemm_block_fp8", bb.cast(A, r), bb.cast(Wt, r, block_m=128), 2048, 4096, 7168,
+               fp8)
     del A, Wt
     # C2 per-tensor: A bf16 (16384, 8192): two reads + one write
     A = torch.randn(16384, 8192, generator=g, device=dev).to(torch.bfloat16)
@@ -494,7 +502,16 @@ def per_recipe(peaks, src):
     r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
     cast_entry("c5_cast_Wt_int4_asym_f32", Wt, r,
                Wt.numel() * 5.5 + Wt.numel() // 128 * 4)
+    sw = bb.cast(Wt, r)
     del Wt
+    for m in (1, 4, 16):
+        A = torch.randn(m, 8192, generator=g, device=dev).to(torch.bfloat16)
+        ms = _time_ms(lambda: bb.linear(A, sw, out_dtype=torch.bfloat16), iters=50)
+        b = 28672 * 8192 // 2 + 2 * (28672 * 64 * 2) + m * 8192 * 2 + m * 28672 * 2
+        gbs = b / (ms * 1e-3) / 1e9
+        res[f"c5_gemv_int4_M{m}"] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
+                                     "TFLOP/s": 2.0 * m * 28672 * 8192 / (ms * 1e-3) / 1e12}
+    del sw
     torch.cuda.empty_cache()
     res["peaks"] = {"hbm_gbs": hbm, "fp8_tflops": fp8, "fp4_tflops": fp4,
                     "source": f"{src} MEASURED_PEAKS.json: hbm_gbs; 2x / 4x "
@@ -502,8 +519,79 @@ def per_recipe(peaks, src):
     return res
 
 
+# --------------------------------------------------------------- ncu cases
+# Small single-kernel cases for `ncu --set full -k regex:<kernel> -c 3`. Each
+# sets up its operands, then launches the kernel 3 times. Operands exceed the
+# 126 MB L2 so DRAM counters stay meaningful, and stay far below a GB.
+
+NCU_CASES = {
+    "gemm_fp8": "per-tensor FP8 GEMM 8192x8192x8192 (A, B 64 MB each) -> bf16",
+    "gemm_mxfp8": "MXFP8 GEMM 8192x8192x8192 -> bf16",
+    "gemm_nvfp4": "NVFP4 GEMM 8192x16384x8192 -> bf16",
+    "gemm_block": "block-FP8 GEMM 2048x4096x7168 (C1) -> f32",
+    "gemv_int4": "INT4 skinny GEMM M=1, W^T 28672x8192 (C5) -> bf16",
+    "cast_pertensor": "per-tensor E4M3 cast, bf16 16384x8192 (amax + apply)",
+    "cast_mxfp8": "MXFP8 cast, bf16 8192x8192",
+    "cast_nvfp4": "NVFP4 cast, bf16 8192x8192",
+    "cast_int4": "INT4 asym g128 cast, f32 8192x8192",
+    "cast_block2d": "128x128 block FP8 cast, f32 4096x7168",
+    "requant_nv_mx": "NVFP4 -> MXFP8 requantize, 8192x8192",
+}
+
+
+def run_ncu_case(name):
+    import torch
+    import breccia_b200 as bb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def bf16(r, c, s=1.0):
+        return (torch.randn(r, c, generator=g, device=dev) * s).to(torch.bfloat16)
+
+    if name.startswith("gemm_") and name != "gemm_block":
+        r = {"gemm_fp8": bb.Float8CurrentScaling(), "gemm_mxfp8": bb.MXFP8BlockScaling(),
+             "gemm_nvfp4": bb.NVFP4BlockScaling()}[name]
+        n = 16384 if name == "gemm_nvfp4" else 8192
+        a, w = bb.cast(bf16(8192, 8192), r), bb.cast(bf16(n, 8192, 0.02), r)
+        fn = lambda: bb.linear(a, w, out_dtype=torch.bfloat16)  # noqa: E731
+    elif name == "gemm_block":
+        r = bb.Float8BlockScaling()
+        a = bb.cast(torch.randn(2048, 7168, generator=g, device=dev), r)
+        w = bb.cast(torch.randn(4096, 7168, generator=g, device=dev) * 0.02, r, block_m=128)
+        fn = lambda: bb.linear(a, w, out_dtype=torch.float32)  # noqa: E731
+    elif name == "gemv_int4":
+        r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
+        w = bb.cast(torch.randn(28672, 8192, generator=g, device=dev) * 0.02, r)
+        a = bf16(1, 8192)
+        fn = lambda: bb.linear(a, w, out_dtype=torch.bfloat16)  # noqa: E731
+    elif name == "requant_nv_mx":
+        st = bb.cast(bf16(8192, 8192), bb.NVFP4BlockScaling())
+        fn = lambda: bb.requantize(st, bb.MXFP8BlockScaling())  # noqa: E731
+    else:
+        x, r, kw = {
+            "cast_pertensor": (lambda: bf16(16384, 8192), bb.Float8CurrentScaling(), {}),
+            "cast_mxfp8": (lambda: bf16(8192, 8192), bb.MXFP8BlockScaling(), {}),
+            "cast_nvfp4": (lambda: bf16(8192, 8192), bb.NVFP4BlockScaling(), {}),
+            "cast_int4": (lambda: torch.randn(8192, 8192, generator=g, device=dev),
+                          bb.INT4Scaling(group_size=128, signed=False, symmetric=False), {}),
+            "cast_block2d": (lambda: torch.randn(4096, 7168, generator=g, device=dev),
+                             bb.Float8BlockScaling(), {"block_m": 128}),
+        }[name]
+        xin = x()
+        fn = lambda: bb.cast(xin, r, **kw)  # noqa: E731
+    torch.cuda.synchronize()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_case": name, "what": NCU_CASES[name], "ok": True}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.ncu_case:
+        return run_ncu_case(args.ncu_case)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -16,6 +16,8 @@ Tensor-core paths (both operands K-major, i.e. ``linear(a, w)`` with ``w`` an
 * NVFP4 x NVFP4 -> ``brc_gemm_nvfp4``
 * Float8BlockScaling 1 x 128 activations x 128 x 128 weights (DeepSeek-v3
   layout, ``cast(w, Float8BlockScaling(), block_m=128)``) -> ``brc_gemm_block_fp8``
+* raw bfloat16 activations (at most 16 rows) x INT4 weight (group 128) ->
+  ``brc_gemm_int4`` (dequantization fused, weight read once)
 """
 
 from __future__ import annotations
@@ -79,6 +81,43 @@ def _tc_pair(a, w):
         if "sf_mma" in sa and "packed" in sa and "sf_mma" in sw and "packed" in sw:
             return "nvfp4"
     return None
+
+
+def _int4_pair(a, w):
+    """Raw bf16 activations (<= 16 rows) x packed INT4 weight (N, K)."""
+    if _is_scaled(a) or not isinstance(a, torch.Tensor) or _name(w) != "int4":
+        return False
+    if not (a.is_cuda and w.data.is_cuda) or a.device != w.data.device:
+        return False
+    if a.dtype != torch.bfloat16 or a.ndim < 1 or w.data.ndim != 2:
+        return False
+    K = a.shape[-1]
+    M = a.numel() // K if K else 0
+    N = w.data.shape[0]
+    return (w.data.shape[1] == K and 0 < M <= 16 and K % 1024 == 0 and N % 16 == 0 and
+            w.recipe.group_size == 128 and "packed" in _side(w.data))
+
+
+def _run_int4(a, w, out_dtype):
+    K = a.shape[-1]
+    M = a.numel() // K
+    N = w.data.shape[0]
+    dev = a.device
+    cdt = out_dtype if out_dtype in _OUT_DT else torch.float32
+    out = torch.empty(a.shape[:-1] + (N,), dtype=cdt, device=dev)
+    a2 = a.contiguous()
+    if a2.data_ptr() % 16:
+        a2 = a2.clone()
+    r = w.recipe
+    sc = w.scale.contiguous()
+    zp = None if w.zero_point is None else w.zero_point.to(sc.dtype).contiguous()
+    with torch.cuda.device(dev):
+        _lib.call("brc_gemm_int4", a2.data_ptr(), M, K, _side(w.data)["packed"].data_ptr(), N,
+                  r.group_size, int(bool(r.signed)), int(bool(r.symmetric)),
+                  _lib.SCALE_F16 if sc.dtype == torch.float16 else _lib.SCALE_F32,
+                  sc.data_ptr(), None if zp is None else zp.data_ptr(), out.data_ptr(),
+                  _OUT_DT[cdt], _stream(dev))
+    return out if cdt == out_dtype else out.to(out_dtype)
 
 
 def _run_tc(kind, a, w, out_dtype, w_codes=None):
@@ -152,6 +191,8 @@ class _ShapeOnly:
 
 def linear(a, w, out_dtype):
     """``a @ w.T`` with ``w`` an ``(N, K)`` operand."""
+    if _int4_pair(a, w):
+        return _run_int4(a, w, out_dtype)
     kind = _tc_pair(a, w)
     if kind is not None:
         return _run_tc(kind, a, w, out_dtype)

@@ -215,6 +215,18 @@ int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int 
 int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
                        int b_fmt, const float* a_scales, const float* b_scales, void* d,
                        int d_dtype, void* stream);
+/* INT4 weight-only skinny GEMM (decode shapes): D[M, N] = A[M, K] * W^T with
+ * A bfloat16 (M <= 16) and W^T the packed INT4 cast of an (N, K) weight (two
+ * codes per byte, element 2i in the low nibble, as brc_cast_int4 writes them)
+ * with scales / zero points (N, K/128) in scale_dtype. The dequantized value
+ * (q - zp) * s is applied per 128-element group: tensor cores form
+ * sum A * (q - zp) exactly per group, the group scale is applied in float32.
+ * group == 128, K % 1024 == 0, N % 16 == 0.
+ * Reference: matmul.py:42-133 (raw activations x dequantized INT4 weight,
+ * cast.py:574-586). */
+int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_packed, int N, int group,
+                  int is_signed, int symmetric, int scale_dtype, const void* scales,
+                  const void* zero_points, void* d, int d_dtype, void* stream);
 /* Sticky device status of the GEMM kernels on the current device (bit 0: a
  * bounded wait timed out and the kernel returned early). Synchronous. */
 int brc_gemm_status(int reset);

@@ -191,3 +191,49 @@ def test_shape_mismatch_raises():
     b = bb().cast(torch.randn(64, 16).cuda(), r)
     with pytest.raises(ValueError, match="shape mismatch"):
         bb().matmul(a, b)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 11])
+@pytest.mark.parametrize("variant", ["asym_fp16", "sym_signed_fp16", "sym_unsigned_fp32",
+                                     "asym_bf16scale"])
+def test_int4_weight_only(M, variant):
+    """Raw bf16 activations x INT4 weight (group 128): the dequant-fused
+    skinny GEMM against the reference's dequantize-then-float32 matmul."""
+    from oracle import cast as ocast
+    from breccia_b200 import gemm
+    from breccia_b200.types import INT4Scaling
+    r = {"asym_fp16": INT4Scaling(group_size=128, signed=False, symmetric=False),
+         "sym_signed_fp16": INT4Scaling(group_size=128),
+         "sym_unsigned_fp32": INT4Scaling(group_size=128, signed=False, scale_dtype="fp32"),
+         "asym_bf16scale": INT4Scaling(group_size=128, signed=False, symmetric=False,
+                                       scale_dtype="bf16")}[variant]
+    N, K = 512, 2048
+    g = torch.Generator().manual_seed(M)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    Wt = torch.randn(N, K, generator=g) * 0.02
+    if variant == "sym_unsigned_fp32":
+        Wt = Wt.abs()
+    sw = bb().cast(Wt.cuda(), r)
+    assert gemm._int4_pair(A.cuda(), sw)
+    out = bb().linear(A.cuda(), sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    qw = ocast.cast(Wt.numpy(), r)
+    ref = ocast.matmul(A.float().numpy(), ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-4)
+
+
+def test_int4_weight_only_config5_shape():
+    """W^T (28672, 8192) f32 ~ N(0, 0.02), asymmetric g128,
+    activations (16, 8192) bf16; checked on a column sample of the output."""
+    from oracle import cast as ocast
+    from breccia_b200.types import INT4Scaling
+    r = INT4Scaling(group_size=128, signed=False, symmetric=False)
+    g = torch.Generator().manual_seed(5)
+    Wt = torch.randn(28672, 8192, generator=g) * 0.02
+    A = torch.randn(16, 8192, generator=g).to(torch.bfloat16)
+    sw = bb().cast(Wt.cuda(), r)
+    out = bb().linear(A.cuda(), sw, out_dtype=torch.bfloat16).float().cpu().numpy()
+    cols = np.arange(0, 28672, 97)
+    qw = ocast.cast(Wt[cols].numpy(), r)
+    ref = ocast.matmul(A.float().numpy(), ocast.dequantize(qw).T)
+    _check(out[:, cols], ref)
