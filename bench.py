@@ -47,7 +47,7 @@ GEMM_DRAM_BYTES = None
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -177,53 +177,67 @@ def make_inputs(device):
 
 
 class Clocks:
-    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+    """SM clock and throttle reasons sampled every 5 ms through NVML (the
+    source nvidia-smi reads) while the timed region runs; nvidia-smi's own
+    200 ms loop is too coarse for a region of a few tens of milliseconds."""
 
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, uuid):
         self.uuid = uuid
-        self.proc = None
+        self.samples = []
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if self.uuid is None or u == self.uuid:
+                    handle = h
+                    break
+            if handle is None:
+                return self
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report no samples
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for ln in (self.out or "").splitlines():
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            if self.uuid and parts[0] != self.uuid:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[4:8]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        active = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v == "Active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows),
-                "sm_max_mhz": max(r[1] for r in rows), "reasons": active, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": "nvml"}
+        active = sorted({n for _, rs in self.samples for n, bit in self.REASONS.items()
+                         if rs & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": getattr(self, "max_mhz", None), "reasons": active,
+                "samples": len(self.samples), "source": "nvml, 5 ms period"}
 
 
 def measured_peaks():

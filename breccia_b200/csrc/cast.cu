@@ -206,12 +206,27 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
   const int part = lane % LPB;
   const int64_t n_warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t n_tiles = (a.n_blocks + BPW - 1) / BPW;
-  for (int64_t tile = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       tile < n_tiles; tile += n_warps) {
+  int64_t tile = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  // The next tile's vectors are loaded before the current tile is encoded, so
+  // each lane keeps two tiles of loads in flight.
+  uint4 vn[NV];
+  auto load_tile = [&](int64_t tl, uint4* dst) {
+    const int64_t b = tl * BPW + lane / LPB;
+    if (tl < n_tiles && b < a.n_blocks) {
+      const char* src = static_cast<const char*>(a.x) + (b * B + (int64_t)part * E) * elem_bytes<DT>();
+#pragma unroll
+      for (int i = 0; i < NV; ++i) dst[i] = ldg16(src + 16 * i);
+    }
+  };
+  load_tile(tile, vn);
+  for (; tile < n_tiles; tile += n_warps) {
     const int64_t blk = tile * BPW + lane / LPB;
     const bool valid = blk < a.n_blocks;
     const int64_t e0 = blk * B + (int64_t)part * E;
     uint4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = vn[i];
+    load_tile(tile + n_warps, vn);
     float st0, st1;  // abs-max, or (min, max) for asymmetric INT4
     if constexpr (MODE == kInt4Asym) {
       st0 = __int_as_float(0x7F800000);
@@ -221,9 +236,6 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       st1 = 0.f;
     }
     if (valid) {
-      const char* src = static_cast<const char*>(a.x) + e0 * elem_bytes<DT>();
-#pragma unroll
-      for (int i = 0; i < NV; ++i) v[i] = ldg16(src + 16 * i);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         if constexpr (MODE == kInt4Asym) vec_minmax<DT>(v[i], st0, st1);
@@ -436,22 +448,22 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
   const char* base = static_cast<const char*>(x);
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (fast) {
-    for (; i + stride < nvec; i += 2 * stride) {
-      const uint4 v0 = ldg16(base + 16 * i);
-      const uint4 v1 = ldg16(base + 16 * (i + stride));
-      float f0[V], f1[V];
-      unpack<DT>(v0, f0);
-      unpack<DT>(v1, f1);
-      uint32_t w0[V / 4], w1[V / 4];
+    // four 16-byte vectors in flight per thread per iteration
+    for (; i + 3 * stride < nvec; i += 4 * stride) {
+      uint4 v[4];
 #pragma unroll
-      for (int j = 0; j < V / 4; ++j) {
-        w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
-                              div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
-        w1[j] = enc4_fp8<FMT>(div_by(f1[4 * j], s, r), div_by(f1[4 * j + 1], s, r),
-                              div_by(f1[4 * j + 2], s, r), div_by(f1[4 * j + 3], s, r));
+      for (int u = 0; u < 4; ++u) v[u] = ldg16(base + 16 * (i + u * stride));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float f0[V];
+        unpack<DT>(v[u], f0);
+        uint32_t w0[V / 4];
+#pragma unroll
+        for (int j = 0; j < V / 4; ++j)
+          w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
+                                div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
+        store_words<V / 4>(codes + (i + u * stride) * V, w0);
       }
-      store_words<V / 4>(codes + i * V, w0);
-      store_words<V / 4>(codes + (i + stride) * V, w1);
     }
     for (; i < nvec; i += stride) {
       float f0[V];
@@ -634,8 +646,30 @@ __global__ void __launch_bounds__(256) k_dequant(DequantArgs a) {
 
 // --------------------------------------------------------------- requantize
 // NVFP4 (unpacked codes + E4M3 scales) -> MXFP8, one lane per 32-element
-// MXFP8 block. Dequantized values are exact float32 products, so this equals
-// cast(dequantize(st), MXFP8BlockScaling(fmt)).
+// MXFP8 block. Every dequantized value e2m1 * e4m3 has at most 6 significant
+// bits and lies in [2^-10, 2688], so it is exact in float16: codes are
+// converted two at a time by the hardware (cvt e2m1x2 -> f16x2), multiplied by
+// the f16 scale and reduced in packed form, and widened to float32 only for
+// the E4M3 encode. The result equals cast(dequantize(st), MXFP8BlockScaling(fmt)).
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t pair_byte) {
+  uint32_t d;
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(d)
+      : "r"(pair_byte));
+  return d;
+}
+__device__ __forceinline__ uint32_t e4m3_to_f16x2_bcast(uint32_t code) {
+  uint32_t d;
+  const uint16_t two = (uint16_t)(code | (code << 8));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(two));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restrict__ codes,
                                                           const uint8_t* __restrict__ scales,
@@ -647,22 +681,36 @@ __global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restr
   for (int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; blk < n_blocks;
        blk += (int64_t)gridDim.x * blockDim.x) {
     const uint4 c0 = ldg16(codes + blk * 32), c1 = ldg16(codes + blk * 32 + 16);
-    const float s0 = dec_e4m3(scales[2 * blk]), s1 = dec_e4m3(scales[2 * blk + 1]);
+    const uint32_t hs0 = e4m3_to_f16x2_bcast(scales[2 * blk]);
+    const uint32_t hs1 = e4m3_to_f16x2_bcast(scales[2 * blk + 1]);
     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    float f[32];
-    float am = 0.f;
+    uint32_t h[16];  // f16x2 values (element 2i low, 2i+1 high)
+    uint32_t amax2 = 0u;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float d = dec_e2m1((w[i >> 2] >> (8 * (i & 3))) & 0xFu);
-      f[i] = __fmul_rn(d, i < 16 ? s0 : s1);
-      am = fmax_nan(am, fabsf(f[i]));
+    for (int i = 0; i < 8; ++i) {
+      // codes are one per byte: byte (b0 | b1 << 4) holds the pair, low nibble first
+      const uint32_t lo = (w[i] & 0x0Fu) | ((w[i] >> 4) & 0xF0u);
+      const uint32_t hi = ((w[i] >> 16) & 0x0Fu) | ((w[i] >> 20) & 0xF0u);
+      const uint32_t sc = i < 4 ? hs0 : hs1;
+      h[2 * i] = h2mul(e2m1x2_to_f16x2(lo), sc);
+      h[2 * i + 1] = h2mul(e2m1x2_to_f16x2(hi), sc);
+      amax2 = f16x2_max_nan(amax2, f16x2_max_nan(h[2 * i] & 0x7FFF7FFFu, h[2 * i + 1] & 0x7FFF7FFFu));
     }
+    const __half2 am2 = *reinterpret_cast<const __half2*>(&amax2);
+    float am = fmax_nan(__low2float(am2), __high2float(am2));
     am = fmax_nan(am, 1e-10f);
     const uint32_t e = e8m0_code(__fdiv_rn(am, kMax), g_e8m0_thr);
     out_scales[blk] = (uint8_t)e;
     if (out_mma) {
       const uint32_t row = fdiv((uint32_t)blk, bpr);
       out_mma[sf_mma_offset(row, (uint32_t)blk - row * bpr.d, sf_col_tiles)] = (uint8_t)e;
+    }
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const __half2 v = *reinterpret_cast<const __half2*>(&h[i]);
+      f[2 * i] = __low2float(v);
+      f[2 * i + 1] = __high2float(v);
     }
     uint32_t o[8];
     if (isfinite(am)) {
@@ -819,7 +867,7 @@ struct PerTensorApply {
     const double fmax = FMT == BRC_FP8_E4M3 ? 448.0 : 57344.0;
     const float floor_scale = (float)(1e-10 / fmax);
     const int V = In<DT>::kVec;
-    const int grid = grid_for(n / V + 1, 256 * 2);
+    const int grid = grid_for(n / V + 1, 256 * 4);
     k_pertensor_apply<DT, FMT><<<grid, 256, 0, st>>>(x, n, amax_bits, floor_scale, codes,
                                                      scale_out);
     return check_launch();

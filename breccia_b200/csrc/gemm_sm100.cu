@@ -494,9 +494,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      // scales for K block kb+1 are loaded while block kb is promoted
+      const float* sa_row = p.bsa + (int64_t)rs * p.bs_ld;
+      const float* sb_row = p.bsb + (int64_t)bgrp * p.bs_ld;
+      float sa_next = sa_row[0], sb_next = sb_row[0];
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        const float s = __fmul_rn(p.bsa[(int64_t)rs * p.bs_ld + kb],
-                                  p.bsb[(int64_t)bgrp * p.bs_ld + kb]);
+        const float s = __fmul_rn(sa_next, sb_next);
+        if (kb + 1 < p.num_kb) {
+          sa_next = sa_row[kb + 1];
+          sb_next = sb_row[kb + 1];
+        }
         if (!mbar_wait(&pfull[pbuf], pphase, abort_flag, p.status, 1u)) {
           ok = false;
           break;

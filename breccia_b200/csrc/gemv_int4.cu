@@ -126,9 +126,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_int4_skinny(const Params p) {
     for (int i = 0; i < 4; ++i) tot[mt][i] = 0.f;
 
   const int nchunks = p.K / KC;
+  const int ngroups = p.K / G;
   load_chunk(0, 0);
   const uint8_t* wrow0 = p.w + (int64_t)(n0 + gid) * kpb + 16 * t;
   const uint8_t* wrow1 = wrow0 + (int64_t)8 * kpb;
+  const int64_t srow0 = (int64_t)(n0 + gid) * groups, srow1 = srow0 + 8 * (int64_t)groups;
+
+  // Prefetch ring: the weight bytes, scales and zero points of the next
+  // PF groups are in flight while the current group is computed (the loop is
+  // latency-bound otherwise: one 32-byte load per thread per group).
+  constexpr int PF = 4;
+  static_assert((KC / G) % PF == 0, "ring must divide the groups of a chunk");
+  uint4 rw0[PF], rw1[PF];
+  float rs0[PF], rs1[PF], rz0[PF], rz1[PF];
+  auto fetch = [&](int grp, int slot_ignored, uint4& a, uint4& b, float& s0, float& s1,
+                   float& z0, float& z1) {
+    (void)slot_ignored;
+    if (active && grp < ngroups) {
+      a = ldg16(wrow0 + (int64_t)grp * 64);
+      b = ldg16(wrow1 + (int64_t)grp * 64);
+      s0 = load_sc(p.scales, srow0 + grp, p.scale_f16);
+      s1 = load_sc(p.scales, srow1 + grp, p.scale_f16);
+      if constexpr (MODE == 2) {
+        z0 = load_sc(p.zp, srow0 + grp, p.scale_f16);
+        z1 = load_sc(p.zp, srow1 + grp, p.scale_f16);
+      }
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < PF; ++i) fetch(i, i, rw0[i], rw1[i], rs0[i], rs1[i], rz0[i], rz1[i]);
 
   for (int c = 0; c < nchunks; ++c) {
     const int buf = c & 1;
@@ -141,21 +167,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_int4_skinny(const Params p) {
     __syncthreads();
     if (active) {
       const __nv_bfloat16* Ab = As + (int64_t)buf * rows_a * ROW;
-#pragma unroll 2
+#pragma unroll
       for (int gg = 0; gg < KC / G; ++gg) {
+        constexpr int kSlots = PF;
+        const int slot = gg % kSlots;
         const int grp = c * (KC / G) + gg;
-        const uint4 w0 = ldg16(wrow0 + (int64_t)grp * 64);
-        const uint4 w1 = ldg16(wrow1 + (int64_t)grp * 64);
-        const int64_t si0 = (int64_t)(n0 + gid) * groups + grp, si1 = si0 + 8 * (int64_t)groups;
-        const float s0 = load_sc(p.scales, si0, p.scale_f16);
-        const float s1 = load_sc(p.scales, si1, p.scale_f16);
+        const uint4 w0 = rw0[slot], w1 = rw1[slot];
+        const float s0 = rs0[slot], s1 = rs1[slot];
         uint32_t off0, off1;
         if constexpr (MODE == 2) {
-          off0 = offset_pair(128.f + load_sc(p.zp, si0, p.scale_f16));
-          off1 = offset_pair(128.f + load_sc(p.zp, si1, p.scale_f16));
+          off0 = offset_pair(128.f + rz0[slot]);
+          off1 = offset_pair(128.f + rz1[slot]);
         } else {
           off0 = off1 = offset_pair(MODE == 1 ? 136.f : 128.f);
         }
+        fetch(grp + PF, slot, rw0[slot], rw1[slot], rs0[slot], rs1[slot], rz0[slot], rz1[slot]);
         const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w};
         const uint32_t r1[4] = {w1.x, w1.y, w1.z, w1.w};
         float acc[MT][4];

@@ -21,7 +21,7 @@ import torch.distributed as dist
 from . import _lib
 from .api import _input, _classes, _stream, _IN_DT, _FMT, _TORCH_FP8
 
-__all__ = ["shard_rows", "cast_per_tensor_sharded", "cast_sharded"]
+__all__ = ["shard_rows", "allreduce_amax_word", "cast_per_tensor_sharded", "cast_sharded"]
 
 
 def shard_rows(n: int, world: int, rank: int, align: int = 128):
@@ -31,6 +31,17 @@ def shard_rows(n: int, world: int, rank: int, align: int = 128):
     per = -(-per // align) * align
     lo = min(n, rank * per)
     return lo, min(n, lo + per)
+
+
+def allreduce_amax_word(word: torch.Tensor, group=None) -> torch.Tensor:
+    """In-place all-reduce(MAX) of a one-element int32 tensor holding the
+    float32 bit pattern of a non-negative amax (or NaN). Non-negative float
+    bit patterns order like integers and NaN's pattern is above +inf's, so the
+    integer maximum is the float maximum with NaN propagating. A no-op outside
+    an initialised process group of more than one rank."""
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group)
+    return word
 
 
 def cast_per_tensor_sharded(x_shard, recipe, group=None):
@@ -48,8 +59,7 @@ def cast_per_tensor_sharded(x_shard, recipe, group=None):
         _lib.call("brc_amax_reset", word.data_ptr(), st)
         _lib.call("brc_amax_accumulate", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
                   word.data_ptr(), st)
-        if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
-            dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group)
+        allreduce_amax_word(word, group)
         _lib.call("brc_cast_pertensor_fp8_apply", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
                   _FMT[fmt], word.data_ptr(), codes.data_ptr(), scale.data_ptr(), st)
     return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe,
