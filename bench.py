@@ -54,8 +54,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--per-recipe", action="store_true",
                     help="also measure every BASELINE config's cast GB/s and GEMM TFLOP/s")
-    ap.add_argument("--cpu-rows", type=int, default=64,
-                    help="rows of A / W^T the CPU baseline encodes per sample")
+    ap.add_argument("--cpu-rows", type=int, default=None,
+                    help="rows of A / W^T the CPU port encodes per sample (default 64 for "
+                         "cpu_baseline, 16 per step for --impl reference)")
     ap.add_argument("--ncu-case", default=None, choices=sorted(NCU_CASES),
                     help="run one kernel on a small case (inputs > L2, < 1 GB) 3 times, for ncu")
     return ap.parse_args()
@@ -120,10 +121,15 @@ def cpu_reference_step(A_np, Wt_np, rows, pool, nproc):
 
 
 def run_reference(args):
-    """--impl reference: the oracle port of breccia's NumPy path on the host."""
+    """--impl reference: the oracle port of breccia's NumPy path on the host.
+    Each step is a bounded sample (16 rows of A and of W^T encoded, about a
+    second of host time) extrapolated to the whole C2 step, so the run stays
+    within minutes for any --steps / --warmup the driver passes."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.cpu_rows is None:
+        args.cpu_rows = 16
     import multiprocessing as mp
     import numpy as np
     from concurrent.futures import ProcessPoolExecutor
@@ -317,30 +323,57 @@ def run_ours(args):
     value = FLOPS / (ms * 1e-3) / 1e12
 
     # ---- end to end through the public API, host buffers
+    # Every step copies its own inputs from pinned host memory and its result
+    # back. The copies run on their own streams and the device buffers are
+    # double-buffered, so step i+1's upload and step i-1's download overlap
+    # step i's kernels, as in a serving loop.
     e2e = None
     if not args.no_e2e:
         A_h = A.cpu().pin_memory()
         W_h = Wt_sh.cpu().pin_memory()
-        out_h = torch.empty((M, n1 - n0), dtype=torch.bfloat16).pin_memory()
-        A_d = torch.empty_like(A)
-        W_d = torch.empty_like(Wt_sh)
+        out_h = [torch.empty((M, n1 - n0), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        A_d = [torch.empty_like(A) for _ in range(2)]
+        W_d = [torch.empty_like(Wt_sh) for _ in range(2)]
+        s_h2d, s_cmp, s_d2h = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+        ev_in = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer b uploaded
+        ev_used = [torch.cuda.Event() for _ in range(2)]  # compute done reading buffer b
+        ev_out = [torch.cuda.Event() for _ in range(2)]   # result of buffer b computed
+        ev_down = [torch.cuda.Event() for _ in range(2)]  # result of buffer b downloaded
+        outs = [None, None]
 
-        def e2e_step():
-            A_d.copy_(A_h, non_blocking=True)
-            W_d.copy_(W_h, non_blocking=True)
-            out = step(A_d, W_d)
-            out_h.copy_(out, non_blocking=True)
+        def e2e_steps(n):
+            for i in range(n):
+                b = i & 1
+                with torch.cuda.stream(s_h2d):
+                    if i >= 2:
+                        s_h2d.wait_event(ev_used[b])
+                    A_d[b].copy_(A_h, non_blocking=True)
+                    W_d[b].copy_(W_h, non_blocking=True)
+                    ev_in[b].record(s_h2d)
+                with torch.cuda.stream(s_cmp):
+                    s_cmp.wait_event(ev_in[b])
+                    if i >= 2:
+                        s_cmp.wait_event(ev_down[b])  # its output buffer is free
+                    outs[b] = step(A_d[b], W_d[b])
+                    ev_used[b].record(s_cmp)
+                    ev_out[b].record(s_cmp)
+                with torch.cuda.stream(s_d2h):
+                    s_d2h.wait_event(ev_out[b])
+                    out_h[b].copy_(outs[b], non_blocking=True)
+                    ev_down[b].record(s_d2h)
 
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
+        e2e_steps(max(2, args.warmup))
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record()
+        e0.record(s_h2d)
+        s_cmp.wait_stream(s_h2d)
+        s_d2h.wait_stream(s_h2d)
+        e2e_steps(args.steps)
+        s_h2d.wait_stream(s_d2h)
+        s_h2d.wait_stream(s_cmp)
+        e1.record(s_h2d)
         torch.cuda.synchronize()
         barrier()
         e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
@@ -348,8 +381,10 @@ def run_ours(args):
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e2e = {"value": FLOPS / (e_ms.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": A_h.numel() * 2 + W_h.numel() * 2,
-               "d2h_bytes_per_step": out_h.numel() * 2,
-               "ms_per_step": e_ms.item()}
+               "d2h_bytes_per_step": out_h[0].numel() * 2,
+               "ms_per_step": e_ms.item(),
+               "pipelining": "uploads, kernels and downloads of consecutive steps overlap "
+                             "(3 streams, 2 buffers)"}
         if world > 1:
             hb = torch.tensor([e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]],
                               device=dev, dtype=torch.float64)
@@ -413,6 +448,8 @@ def _warm_pool(pool, nproc):
 
 def cpu_baseline(args):
     """Rank 0, N = 1: the oracle port of the reference, bounded sample."""
+    if args.cpu_rows is None:
+        args.cpu_rows = 64
     import multiprocessing as mp
     from concurrent.futures import ProcessPoolExecutor
     A_np, Wt_np = host_inputs_numpy()
@@ -431,16 +468,32 @@ def cpu_baseline(args):
 # --------------------------------------------------------------- per recipe
 
 
-def _time_ms(fn, iters=10, warm=3):
+def _time_ms(fn, iters=10, warm=3, graph=True):
+    """Device time per call. With graph=True the call is captured once in a
+    CUDA graph and replayed, so small kernels are timed without the Python
+    launch overhead of the wrapper (the GPU would otherwise idle between
+    launches); each replay runs the same kernels with the same arguments."""
     import torch
     for _ in range(warm):
         fn()
+    torch.cuda.synchronize()
+    run = fn
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        run = g.replay
+        run()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
     for _ in range(iters):
-        fn()
+        run()
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / iters

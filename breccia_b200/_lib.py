@@ -31,7 +31,7 @@ PROTOTYPES = {
     "brc_cast_block_fp8_2d": ([_p, _i, _i64, _i64, _i, _i, _i, _p, _p, _p], _i),
     "brc_cast_mxfp8": ([_p, _i, _i64, _i64, _i, _p, _p, _p, _p], _i),
     "brc_cast_nvfp4": ([_p, _i, _i64, _i64, _p, _p, _p, _p, _p], _i),
-    "brc_cast_int4": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p, _p, _p, _p], _i),
+    "brc_cast_int4": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "brc_dequant_pertensor_fp8": ([_p, _i64, _i, _p, _p, _i, _p], _i),
     "brc_dequant_block_fp8": ([_p, _i64, _i64, _i, _i, _i, _p, _p, _i, _p], _i),
     "brc_dequant_mxfp8": ([_p, _i64, _i64, _i, _p, _p, _i, _p], _i),
@@ -43,7 +43,7 @@ PROTOTYPES = {
     "brc_gemm_mxfp8": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_nvfp4": ([_p, _p, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_block_fp8": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
-    "brc_gemm_int4": ([_p, _i, _i, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
+    "brc_gemm_int4": ([_p, _i, _i, _p, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_status": ([_i], _i),
 }
 

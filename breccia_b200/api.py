@@ -214,17 +214,23 @@ def _cast_int4(x, recipe, ST, L, st):
     K = _last_axis_checks(x, "INT4Scaling", G, "group_size")
     rows = x.numel() // K if K else 0
     sdt = torch.float16 if recipe.scale_dtype == "fp16" else torch.float32  # cast.py:512-513
-    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
-    packed = torch.empty(x.shape[:-1] + (K // 2,), dtype=torch.uint8, device=x.device) \
-        if G % 2 == 0 else None
-    scale = torch.empty(x.shape[:-1] + (K // G,), dtype=sdt, device=x.device)
+    dev = x.device
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
+    scale = torch.empty(x.shape[:-1] + (K // G,), dtype=sdt, device=dev)
     zp = None if recipe.symmetric else torch.empty_like(scale)
+    # the skinny-GEMM tile layout, when the weight shape allows it
+    tiles = stiles = ztiles = None
+    if G == 128 and rows % 16 == 0 and rows > 0:
+        tiles = torch.empty(rows * K // 2, dtype=torch.uint8, device=dev)
+        stiles = torch.empty(rows * (K // G), dtype=torch.float32, device=dev)
+        ztiles = None if recipe.symmetric else torch.empty_like(stiles)
     _lib.call("brc_cast_int4", x.data_ptr(), _IN_DT[x.dtype], rows, K, G,
               int(bool(recipe.signed)), int(bool(recipe.symmetric)),
               _lib.SCALE_F16 if sdt == torch.float16 else _lib.SCALE_F32,
-              codes.data_ptr(), _ptr(packed), scale.data_ptr(), _ptr(zp), st)
-    if packed is not None:
-        _remember(codes, packed=packed)
+              codes.data_ptr(), None, scale.data_ptr(), _ptr(zp), _ptr(tiles), _ptr(stiles),
+              _ptr(ztiles), st)
+    if tiles is not None:
+        _remember(codes, int4_tiles=tiles, int4_scale_tiles=stiles, int4_zp_tiles=ztiles)
     return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockK(block_size=G),
               zero_point=zp)
 
@@ -350,8 +356,9 @@ def linear(a, w, out_dtype=torch.bfloat16):
 
 
 def gemm_operands(scaled) -> dict:
-    """Tensor-core side data recorded by ``cast`` for ``scaled``: ``sf_mma``
-    (scales in the tcgen05 layout) and/or ``packed`` (two 4-bit codes per byte,
-    element 2i in the low nibble)."""
+    """Side data recorded by ``cast`` for ``scaled``: ``sf_mma`` (scales in
+    the tcgen05 layout), ``packed`` (two 4-bit codes per byte, element 2i in
+    the low nibble), or the INT4 skinny-GEMM tiles (``int4_tiles``,
+    ``int4_scale_tiles``, ``int4_zp_tiles``)."""
     return dict(_side(scaled.data if scaled.data.dtype == torch.uint8
                       else scaled.data))

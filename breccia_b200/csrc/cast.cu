@@ -110,6 +110,11 @@ struct BlockCastArgs {
   uint32_t sf_col_tiles;
   int is_signed;
   int scale_f16;
+  // INT4, group 128, rows % 16 == 0: the skinny-GEMM layout (16-row x 128
+  // element tiles of packed codes, fp32 scales / zero points per tile row)
+  uint8_t* packed_tiles;
+  float* scale_tiles;
+  float* zp_tiles;
 };
 
 template <int E>
@@ -120,7 +125,7 @@ struct LaneVals {
 // Encode one lane's E values given the block's scale; writes codes/packed.
 template <int MODE, int FMT, int E>
 __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, const float* f,
-                                            float s, float zp, bool fast) {
+                                            float s, float zp, bool fast, int64_t tile_off) {
   constexpr int NW = E / 4;
   uint32_t w[NW];
   if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
@@ -192,6 +197,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
     if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
+    if (a.packed_tiles) store_packed<NW>(a.packed_tiles + tile_off, w);
   }
 }
 
@@ -319,7 +325,26 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       }
       fast = isfinite(s) && isfinite(zp);
     }
-    encode_lane<MODE, FMT, E>(a, e0, f, s, zp, fast);
+    int64_t tile_off = 0;
+    if constexpr (MODE == kInt4Sym || MODE == kInt4Asym) {
+      if (a.packed_tiles) {
+        // tile (row / 16, group) of 16 rows x 64 bytes; one fp32 scale / zero
+        // point (the stored value) per tile row
+        const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
+        const uint32_t g = (uint32_t)blk - row * a.blocks_per_row.d;
+        const int64_t tile = (int64_t)(row >> 4) * a.blocks_per_row.d + g;
+        tile_off = tile * 1024 + (row & 15) * 64 + (part * E) / 2;
+        if (part == 0) {
+          const float sv = a.scale_f16 ? __half2float(to_half_canon(s)) : canon_nan(s);
+          a.scale_tiles[tile * 16 + (row & 15)] = sv;
+          if constexpr (MODE == kInt4Asym) {
+            const float zv = a.scale_f16 ? __half2float(to_half_canon(zp)) : canon_nan(zp);
+            a.zp_tiles[tile * 16 + (row & 15)] = zv;
+          }
+        }
+      }
+    }
+    encode_lane<MODE, FMT, E>(a, e0, f, s, zp, fast, tile_off);
   }
 }
 
@@ -982,7 +1007,8 @@ int brc_cast_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t cols, uint8
 
 int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int group,
                   int is_signed, int symmetric, int scale_dtype, uint8_t* codes,
-                  uint8_t* packed, void* scales, void* zero_points, void* stream) {
+                  uint8_t* packed, void* scales, void* zero_points, uint8_t* packed_tiles,
+                  float* scale_tiles, float* zp_tiles, void* stream) {
   int rc = common_checks(x, x_dtype, rows, cols, group);
   if (rc) return rc;
   if (!symmetric && is_signed) return BRC_ERR_UNSUPPORTED;
@@ -991,11 +1017,19 @@ int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int gr
   if (!scales || (!codes && !packed)) return BRC_ERR_NULL;
   if (!symmetric && !zero_points) return BRC_ERR_NULL;
   if ((codes && !aligned16(codes)) || (packed && !aligned16(packed))) return BRC_ERR_ALIGN;
+  if (packed_tiles) {
+    if (group != 128 || rows % 16 || !scale_tiles || (!symmetric && !zp_tiles))
+      return BRC_ERR_UNSUPPORTED;
+    if (!aligned16(packed_tiles)) return BRC_ERR_ALIGN;
+  }
   BlockCastArgs a = make_args(x, rows, cols, group);
   a.codes = codes;
   a.packed = packed;
   a.scales = scales;
   a.zp = zero_points;
+  a.packed_tiles = packed_tiles;
+  a.scale_tiles = scale_tiles;
+  a.zp_tiles = zp_tiles;
   a.is_signed = is_signed ? 1 : 0;
   a.scale_f16 = scale_dtype == BRC_SCALE_F16;
   cudaStream_t st = (cudaStream_t)stream;

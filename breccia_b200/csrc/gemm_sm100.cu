@@ -662,16 +662,31 @@ Params base_params(int M, int N, int K, int k_per_stage, void* d) {
 }  // namespace gemm
 }  // namespace brc
 
+namespace brc {
+// Device address of the sticky GEMM status word, for kernels in other
+// translation units. Looked up once per device (with that device current) and
+// cached, so later launches make no runtime lookups.
+uint32_t* gemm_status_ptr() {
+  static std::mutex mu;
+  static uint32_t* cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    uint32_t* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_gemm_status) != cudaSuccess)
+      return nullptr;
+    cache[dev] = p;
+  }
+  return cache[dev];
+}
+}  // namespace brc
+
 using namespace brc;
 using namespace brc::gemm;
 
 namespace {
-uint32_t* status_word() {
-  uint32_t* p = nullptr;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_gemm_status) != cudaSuccess)
-    return nullptr;
-  return p;
-}
+uint32_t* status_word() { return brc::gemm_status_ptr(); }
 }  // namespace
 
 extern "C" {

@@ -51,28 +51,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread is suspended (issuing nothing)
+// until the phase completes or about `hint_ns` elapse.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Every wait in the GEMMs is bounded. After kWaitLimitNs the waiter records
 // `code` in the status word, raises the CTA's abort flag and returns false;
 // the other roles see the flag and wind down (draining their own in-flight
-// copies and MMAs) so the kernel always terminates.
+// copies and MMAs) so the kernel always terminates. Waiting threads sleep in
+// the barrier (suspend-time hint) instead of spinning, so they take no issue
+// slots from the warps doing work.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSleepHintNs = 20000;          // re-check abort / deadline every ~20 us
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile uint32_t* abort_flag, uint32_t* status,
                                           uint32_t code) {
-#pragma unroll 1
-  for (int i = 0; i < 256; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kSleepHintNs)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > kWaitLimitNs) {
       *abort_flag = 1u;
       if (status) atomicOr(status, code);
       return false;
     }
-    __nanosleep(64);
   }
 }
 

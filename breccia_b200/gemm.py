@@ -95,7 +95,7 @@ def _int4_pair(a, w):
     M = a.numel() // K if K else 0
     N = w.data.shape[0]
     return (w.data.shape[1] == K and 0 < M <= 16 and K % 1024 == 0 and N % 16 == 0 and
-            w.recipe.group_size == 128 and "packed" in _side(w.data))
+            w.recipe.group_size == 128 and "int4_tiles" in _side(w.data))
 
 
 def _run_int4(a, w, out_dtype):
@@ -109,14 +109,13 @@ def _run_int4(a, w, out_dtype):
     if a2.data_ptr() % 16:
         a2 = a2.clone()
     r = w.recipe
-    sc = w.scale.contiguous()
-    zp = None if w.zero_point is None else w.zero_point.to(sc.dtype).contiguous()
+    side = _side(w.data)
+    zt = side["int4_zp_tiles"]
     with torch.cuda.device(dev):
-        _lib.call("brc_gemm_int4", a2.data_ptr(), M, K, _side(w.data)["packed"].data_ptr(), N,
-                  r.group_size, int(bool(r.signed)), int(bool(r.symmetric)),
-                  _lib.SCALE_F16 if sc.dtype == torch.float16 else _lib.SCALE_F32,
-                  sc.data_ptr(), None if zp is None else zp.data_ptr(), out.data_ptr(),
-                  _OUT_DT[cdt], _stream(dev))
+        _lib.call("brc_gemm_int4", a2.data_ptr(), M, K, side["int4_tiles"].data_ptr(), N,
+                  int(bool(r.signed)), int(bool(r.symmetric)),
+                  side["int4_scale_tiles"].data_ptr(), None if zt is None else zt.data_ptr(),
+                  out.data_ptr(), _OUT_DT[cdt], _stream(dev))
     return out if cdt == out_dtype else out.to(out_dtype)
 
 

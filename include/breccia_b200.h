@@ -145,10 +145,17 @@ int brc_cast_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t cols, uint8
  * stores as float32). zero_points is required iff !symmetric.
  * codes (optional): one code per byte (low nibble). packed (optional): two
  * per byte, element 2i in the LOW nibble.
+ * packed_tiles / scale_tiles / zp_tiles (optional; group == 128 and
+ * rows % 16 == 0): the layout brc_gemm_int4 streams. Tile (r/16, g) of
+ * 16 rows x 128 elements is 1024 bytes at ((r/16) * (cols/128) + g) * 1024,
+ * row r%16 at +64*(r%16), codes packed as above; scale_tiles / zp_tiles hold
+ * the stored scale / zero point as float32 at ((r/16) * (cols/128) + g) * 16
+ * + r%16. zp_tiles is required iff !symmetric.
  */
 int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int group,
                   int is_signed, int symmetric, int scale_dtype, uint8_t* codes,
-                  uint8_t* packed, void* scales, void* zero_points, void* stream);
+                  uint8_t* packed, void* scales, void* zero_points, uint8_t* packed_tiles,
+                  float* scale_tiles, float* zp_tiles, void* stream);
 
 /* ======================================================= dequantize
  * out = decode(code) * scale (asymmetric INT4: (code - zp) * scale), written as
@@ -216,17 +223,16 @@ int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, 
                        int b_fmt, const float* a_scales, const float* b_scales, void* d,
                        int d_dtype, void* stream);
 /* INT4 weight-only skinny GEMM (decode shapes): D[M, N] = A[M, K] * W^T with
- * A bfloat16 (M <= 16) and W^T the packed INT4 cast of an (N, K) weight (two
- * codes per byte, element 2i in the low nibble, as brc_cast_int4 writes them)
- * with scales / zero points (N, K/128) in scale_dtype. The dequantized value
- * (q - zp) * s is applied per 128-element group: tensor cores form
- * sum A * (q - zp) exactly per group, the group scale is applied in float32.
- * group == 128, K % 1024 == 0, N % 16 == 0.
+ * A bfloat16 (M <= 16) and W^T an (N, K) weight cast by brc_cast_int4 with
+ * group 128, given in its tile layout (packed_tiles, scale_tiles, zp_tiles;
+ * zp_tiles NULL for symmetric recipes). Per 128-element group the tensor
+ * cores form sum A * (q - zp) and the group scale is applied in float32.
+ * K % 1024 == 0, N % 16 == 0.
  * Reference: matmul.py:42-133 (raw activations x dequantized INT4 weight,
  * cast.py:574-586). */
-int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_packed, int N, int group,
-                  int is_signed, int symmetric, int scale_dtype, const void* scales,
-                  const void* zero_points, void* d, int d_dtype, void* stream);
+int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_tiles, int N, int is_signed,
+                  int symmetric, const float* scale_tiles, const float* zp_tiles, void* d,
+                  int d_dtype, void* stream);
 /* Sticky device status of the GEMM kernels on the current device (bit 0: a
  * bounded wait timed out and the kernel returned early). Synchronous. */
 int brc_gemm_status(int reset);

@@ -56,7 +56,8 @@ def test_null_pointers_rejected():
     assert L.brc_cast_mxfp8(p, 0, 4, 64, 0, None, p, None, None) == _lib.BRC_ERR_NULL
     assert L.brc_cast_nvfp4(p, 0, 4, 64, None, None, p, None, None) == _lib.BRC_ERR_NULL
     # asymmetric INT4 needs a zero-point buffer
-    assert L.brc_cast_int4(p, 0, 4, 128, 128, 0, 0, 0, p, None, p, None, None) == _lib.BRC_ERR_NULL
+    assert L.brc_cast_int4(p, 0, 4, 128, 128, 0, 0, 0, p, None, p, None, None, None, None,
+                           None) == _lib.BRC_ERR_NULL
 
 
 def test_shapes_dtypes_alignment_rejected():
@@ -67,8 +68,8 @@ def test_shapes_dtypes_alignment_rejected():
     assert L.brc_cast_block_fp8(p, 7, 4, 128, 128, 0, p, p, None) == _lib.BRC_ERR_DTYPE
     assert L.brc_cast_block_fp8(p, 0, 4, 128, 128, 9, p, p, None) == _lib.BRC_ERR_DTYPE
     assert L.brc_cast_block_fp8(p + 4, 0, 4, 128, 128, 0, p, p, None) == _lib.BRC_ERR_ALIGN
-    assert L.brc_cast_int4(p, 0, 4, 128, 128, 1, 0, 0, p, None, p, p, None) == \
-        _lib.BRC_ERR_UNSUPPORTED  # asymmetric + signed is not a valid recipe
+    assert L.brc_cast_int4(p, 0, 4, 128, 128, 1, 0, 0, p, None, p, p, None, None, None,
+                           None) == _lib.BRC_ERR_UNSUPPORTED  # asymmetric + signed is invalid
     assert L.brc_dequant_nvfp4(p, 4, 24, p, p, 0, None) == _lib.BRC_ERR_SHAPE
     assert L.brc_dequant_mxfp8(p, 4, 64, 0, p, p, 5, None) == _lib.BRC_ERR_DTYPE
 
