@@ -6,11 +6,17 @@ Headline workload (Float8CurrentScaling E4M3):
   W bf16 (8192, 8192) ~ N(0,0.02), held as W^T (N, K) (nn.Linear orientation).
   One step = per-tensor cast of A + per-tensor cast of W^T + the 16384 x 8192 x
   8192 tcgen05 FP8 GEMM -> bf16.
-  N GPUs: W^T is split along N (rows); the weight's amax is reduced with one
-  NCCL all-reduce(MAX) of 4 bytes; A is replicated; each rank computes its
-  C[:, shard]. Total work is fixed ("strong" scaling).
+  N GPUs, default (--shard batch, data parallel, "weak" scaling): every rank
+  holds its own batch of 16384 activation rows (rank 0's is the C2 A above,
+  the others are seeded per rank) and the whole weight. The activations'
+  per-tensor scale is that of the concatenated global batch (16384*N rows):
+  one NCCL all-reduce(MAX) of a 4-byte amax word, overlapped with the
+  weight's cast. Per-GPU work is fixed as N grows.
+  --shard weight ("strong" scaling): W^T is split along N (rows); the
+  weight's amax is reduced with one all-reduce; A is replicated; each rank
+  computes its C[:, shard]. Total work is fixed.
 
-value = 2*M*N*K / step time (max over ranks), whole job.
+value = total 2*M*N*K over all ranks / step time (max over ranks).
 e2e   = the same through the public API with the inputs copied from pinned
         host memory and the output C copied back inside every step.
 
@@ -50,6 +56,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shard", default="batch", choices=["batch", "weight"],
+                    help="N>1 layout: per-rank activation batches with the weight replicated "
+                         "(weak scaling, default) or the weight split along N (strong)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--per-recipe", action="store_true",
@@ -171,14 +180,24 @@ def host_inputs_numpy():
 # --------------------------------------------------------------- GPU side
 
 
-def make_inputs(device):
+def _make_a(g, device):
     import torch
-    g = torch.Generator(device=device).manual_seed(0)
     A = torch.randn(M, K, generator=g, device=device)
     mask = torch.rand(M, K, generator=g, device=device) < 0.001
     A = torch.where(mask, torch.randn(M, K, generator=g, device=device) * 50, A)
-    A = A.to(torch.bfloat16)
+    return A.to(torch.bfloat16)
+
+
+def make_inputs(device, batch_seed=None):
+    """C2's A and W^T (seed 0). With ``batch_seed`` the returned A is instead
+    a fresh batch of the same distribution from that seed (W^T unchanged)."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(0)
+    A = _make_a(g, device)
     W = (torch.randn(K, N, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    if batch_seed is not None:
+        del A
+        A = _make_a(torch.Generator(device=device).manual_seed(batch_seed), device)
     return A, W.t().contiguous()
 
 
@@ -260,7 +279,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     import breccia_b200 as bb
-    from breccia_b200.dist import shard_rows, cast_per_tensor_sharded
+    from breccia_b200.dist import shard_rows, cast_per_tensor_sharded, cast_per_tensor_async
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -272,11 +291,13 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     recipe = bb.Float8CurrentScaling(fp8_format="E4M3")
-    A, Wt = make_inputs(dev)
-    n0, n1 = shard_rows(N, world, rank)
+    batch = args.shard == "batch"
+    A, Wt = make_inputs(dev, batch_seed=(1000 + rank) if batch and rank > 0 else None)
+    n0, n1 = (0, N) if batch else shard_rows(N, world, rank)
     Wt_sh = Wt[n0:n1].contiguous()
     del Wt
     torch.cuda.synchronize()
+    job_flops = FLOPS * (world if batch else 1)
 
     def barrier():
         if world > 1:
@@ -285,8 +306,15 @@ def run_ours(args):
     gemm_events = []
 
     def step(a_in, w_in, record=False):
-        sa = bb.cast(a_in, recipe)
-        sw = cast_per_tensor_sharded(w_in, recipe)
+        if batch:
+            # activations: global amax over all ranks' batches, its all-reduce
+            # in flight while the (replicated) weight is cast
+            pending = cast_per_tensor_async(a_in, recipe)
+            sw = bb.cast(w_in, recipe)
+            sa = pending.wait()
+        else:
+            sa = bb.cast(a_in, recipe)
+            sw = cast_per_tensor_sharded(w_in, recipe)
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
@@ -320,7 +348,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms, gemm_ms_max = ms_t.tolist()
-    value = FLOPS / (ms * 1e-3) / 1e12
+    value = job_flops / (ms * 1e-3) / 1e12
 
     # ---- end to end through the public API, host buffers
     # Every step copies its own inputs from pinned host memory and its result
@@ -379,7 +407,7 @@ def run_ours(args):
         e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": FLOPS / (e_ms.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
+        e2e = {"value": job_flops / (e_ms.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": A_h.numel() * 2 + W_h.numel() * 2,
                "d2h_bytes_per_step": out_h[0].numel() * 2,
                "ms_per_step": e_ms.item(),
@@ -421,17 +449,23 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak" if batch else "strong",
+            "vs_baseline": None,
             "dtype": "e4m3 x e4m3 -> f32 accumulate -> bf16 out",
             "data": "synthetic (seeded torch generator, BASELINE configs[1] shapes/distributions)",
-            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K,
+            "config": {"workload": WORKLOAD, "M": M * (world if batch else 1), "N": N, "K": K,
+                       "M_per_gpu": M,
                        "parallelism": "single GPU" if world == 1 else
+                       (f"data parallel over {world} GPUs: {M} activation rows per GPU, W "
+                        "replicated, one NCCL all-reduce(MAX) of the activations' amax "
+                        "(overlapped with the weight cast)") if batch else
                        f"W^T split along N over {world} GPUs, A replicated, "
                        "one NCCL all-reduce(MAX) of the weight amax",
                        "l2": "inputs larger than L2 (A is 268 MB)"},
             "clocks": clk.summary(),
             "e2e": e2e,
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 7 * args.steps * world,
+            "gpu_launches_per_rank": 7 * args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu,
         }

@@ -1,6 +1,6 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core GEMMs:
-// mbarriers (with bounded waits), TMA tensor and bulk copies (never with
-// cluster multicast), and the tcgen05 family (TMEM alloc, MMA, commit,
+// mbarriers (with bounded waits), TMA tensor and bulk copies (each CTA
+// loads its own tiles), and the tcgen05 family (TMEM alloc, MMA, commit,
 // TMEM -> register loads, SMEM -> TMEM scale-factor copies).
 //
 // Descriptor bit layouts follow the PTX ISA's tcgen05 "shared memory

@@ -1,7 +1,15 @@
 """Sharding across the GPUs of one node (one process per GPU, torch.distributed).
 
 The reference is single-process; these helpers are the multi-GPU form of its
-hot path. Weights are split along N (the output dimension): each rank holds
+hot path. Two layouts use them.
+
+Data parallel (bench.py's default for N > 1): each rank holds its own batch of
+activation rows and the whole weight. The activations' per-tensor scale is the
+one of the concatenated batch, so the local amax words are all-reduced; the
+weight's cast is local. ``cast_per_tensor_async`` lets that all-reduce overlap
+the weight's cast.
+
+Weight split: weights are split along N (the output dimension): each rank holds
 ``W^T[n0:n1, :]`` (rows of the nn.Linear-oriented weight), casts it, and
 computes ``C[:, n0:n1] = A @ W^T[n0:n1, :]^T``. Block recipes need no
 communication (their blocks run along K, inside one rank's rows). Per-tensor
@@ -21,7 +29,8 @@ import torch.distributed as dist
 from . import _lib
 from .api import _input, _classes, _stream, _IN_DT, _FMT, _TORCH_FP8
 
-__all__ = ["shard_rows", "allreduce_amax_word", "cast_per_tensor_sharded", "cast_sharded"]
+__all__ = ["shard_rows", "allreduce_amax_word", "cast_per_tensor_sharded", "cast_sharded",
+           "cast_per_tensor_async", "PendingCast"]
 
 
 def shard_rows(n: int, world: int, rank: int, align: int = 128):
@@ -44,26 +53,62 @@ def allreduce_amax_word(word: torch.Tensor, group=None) -> torch.Tensor:
     return word
 
 
-def cast_per_tensor_sharded(x_shard, recipe, group=None):
-    """Per-tensor FP8 cast of this rank's shard with the global amax of all
-    ranks' shards (one NCCL all-reduce of 4 bytes)."""
+class PendingCast:
+    """A per-tensor FP8 cast whose amax all-reduce is in flight.
+
+    ``cast_per_tensor_async`` reduces the local shard's amax and starts the
+    all-reduce without making the current stream wait for it, so independent
+    work issued next (the weight's cast, say) overlaps the collective.
+    ``wait()`` makes the current stream wait for the reduced amax, encodes the
+    shard and returns its ScaledTensor."""
+
+    def __init__(self, x, recipe, word, work):
+        self._x, self._recipe, self._word, self._work = x, recipe, word, work
+
+    def wait(self):
+        if self._work is not None:
+            self._work.wait()
+            self._work = None
+        x, recipe = self._x, self._recipe
+        ST, L = _classes(recipe)
+        dev = x.device
+        fmt = recipe.fp8_format
+        codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
+        scale = torch.empty((), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("brc_cast_pertensor_fp8_apply", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
+                      _FMT[fmt], self._word.data_ptr(), codes.data_ptr(), scale.data_ptr(),
+                      _stream(dev))
+        return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe,
+                  layout=L.PerTensor())
+
+
+def cast_per_tensor_async(x_shard, recipe, group=None) -> PendingCast:
+    """Start a per-tensor FP8 cast of this rank's shard with the global amax
+    of all ranks' shards: the local amax is reduced on the current stream and
+    its 4-byte all-reduce(MAX) is launched asynchronously (no collective
+    outside an initialised process group of more than one rank)."""
     x = _input(x_shard)
-    ST, L = _classes(recipe)
+    if getattr(recipe, "name", None) not in ("delayed", "current"):
+        raise ValueError("cast_per_tensor_async takes a per-tensor recipe "
+                         "(DelayedScaling or Float8CurrentScaling)")
     dev = x.device
-    fmt = recipe.fp8_format
-    codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
-    scale = torch.empty((), dtype=torch.float32, device=dev)
     word = torch.empty(1, dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         st = _stream(dev)
         _lib.call("brc_amax_reset", word.data_ptr(), st)
         _lib.call("brc_amax_accumulate", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
                   word.data_ptr(), st)
-        allreduce_amax_word(word, group)
-        _lib.call("brc_cast_pertensor_fp8_apply", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
-                  _FMT[fmt], word.data_ptr(), codes.data_ptr(), scale.data_ptr(), st)
-    return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe,
-              layout=L.PerTensor())
+    work = None
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        work = dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group, async_op=True)
+    return PendingCast(x, recipe, word, work)
+
+
+def cast_per_tensor_sharded(x_shard, recipe, group=None):
+    """Per-tensor FP8 cast of this rank's shard with the global amax of all
+    ranks' shards (one NCCL all-reduce of 4 bytes)."""
+    return cast_per_tensor_async(x_shard, recipe, group).wait()
 
 
 def cast_sharded(x_shard, recipe, group=None, **kw):
