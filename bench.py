@@ -45,9 +45,11 @@ WORKLOAD = ("C2 Float8CurrentScaling E4M3 per-tensor: A bf16 (16384, 8192) N(0,1
             "+ 16384x8192x8192 tcgen05 FP8 GEMM -> bf16")
 METRIC = "scaled-matmul TFLOP/s (C2 per-tensor FP8: cast A + cast W + GEMM, whole job)"
 
-# DRAM bytes per launch of the GEMM kernel from one ncu capture of this
-# workload (profiles/gemm_fp8_pertensor_c2.txt); None until captured.
-GEMM_DRAM_BYTES = None
+# DRAM bytes (read + write) of one launch of the GEMM kernel on this
+# workload, from one ncu capture of `bench.py --steps 2 --warmup 3 --no-e2e
+# --no-cpu-baseline` (dram__bytes_read.sum 663.62 MB + dram__bytes_write.sum
+# 246.02 MB; profiles/gemm_fp8_pertensor_c2.txt).
+GEMM_DRAM_BYTES = 663.62e6 + 246.02e6
 
 
 def parse():

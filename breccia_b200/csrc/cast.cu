@@ -473,33 +473,33 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
   const char* base = static_cast<const char*>(x);
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (fast) {
-    // four 16-byte vectors in flight per thread per iteration
-    for (; i + 3 * stride < nvec; i += 4 * stride) {
-      uint4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = ldg16(base + 16 * (i + u * stride));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float f0[V];
-        unpack<DT>(v[u], f0);
-        uint32_t w0[V / 4];
-#pragma unroll
-        for (int j = 0; j < V / 4; ++j)
-          w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
-                                div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
-        store_words<V / 4>(codes + (i + u * stride) * V, w0);
-      }
-    }
-    for (; i < nvec; i += stride) {
+    // Vectors are visited from the end of the tensor backwards: the amax
+    // pass that ran just before read it front to back, so its tail is still
+    // in L2 and is consumed first. Input lines are read here for the last
+    // time and the codes are not read back by this kernel, so both carry an
+    // evict-first policy and leave the cached tail in place.
+    const uint64_t pol = l2_evict_first_policy();
+    auto encode_store = [&](const uint4 v, int64_t vi) {
       float f0[V];
-      unpack<DT>(ldg16(base + 16 * i), f0);
+      unpack<DT>(v, f0);
       uint32_t w0[V / 4];
 #pragma unroll
       for (int j = 0; j < V / 4; ++j)
         w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
                               div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
-      store_words<V / 4>(codes + i * V, w0);
+      if constexpr (V == 8) stg8_last_use(codes + vi * V, w0[0], w0[1], pol);
+      else *reinterpret_cast<uint32_t*>(codes + vi * V) = w0[0];
+    };
+    // four 16-byte vectors in flight per thread per iteration
+    for (; i + 3 * stride < nvec; i += 4 * stride) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = ldg16_last_use(base + 16 * (nvec - 1 - (i + u * stride)), pol);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) encode_store(v[u], nvec - 1 - (i + u * stride));
     }
+    for (; i < nvec; i += stride)
+      encode_store(ldg16_last_use(base + 16 * (nvec - 1 - i), pol), nvec - 1 - i);
   } else {
     for (; i < nvec; i += stride) {
       float f0[V];
@@ -819,7 +819,8 @@ int launch_block(const BlockCastArgs& a, int B, cudaStream_t st) {
   }
   if (MODE == kBlockFp8 || MODE == kInt4Sym || MODE == kInt4Asym) {
     if (a.packed && (B & 1)) return BRC_ERR_UNSUPPORTED;
-    k_block_cast_generic<DT, MODE, FMT><<<grid_for(a.n_blocks, 256), 256, 0, st>>>(a, B);
+    k_block_cast_generic<DT, MODE, FMT>
+        <<<grid_for(a.n_blocks, 256), 256, 0, st>>>(a, B);
     return check_launch();
   }
   return BRC_ERR_UNSUPPORTED;
@@ -875,11 +876,11 @@ int brc_amax_accumulate(const void* x, int x_dtype, int64_t n, uint32_t* amax_bi
   if (n == 0) return BRC_OK;
   if (!aligned16(x)) return BRC_ERR_ALIGN;
   const int V = x_dtype == BRC_DTYPE_F32 ? 4 : 8;
-  const int grid = grid_for(n / V + 1, 256 * 4);
   cudaStream_t st = (cudaStream_t)stream;
-  if (x_dtype == BRC_DTYPE_F32) k_amax<BRC_DTYPE_F32><<<grid, 256, 0, st>>>(x, n, amax_bits);
-  else if (x_dtype == BRC_DTYPE_BF16) k_amax<BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(x, n, amax_bits);
-  else k_amax<BRC_DTYPE_F16><<<grid, 256, 0, st>>>(x, n, amax_bits);
+  auto kern = x_dtype == BRC_DTYPE_F32    ? k_amax<BRC_DTYPE_F32>
+              : x_dtype == BRC_DTYPE_BF16 ? k_amax<BRC_DTYPE_BF16>
+                                          : k_amax<BRC_DTYPE_F16>;
+  kern<<<grid_for(n / V + 1, 256 * 4), 256, 0, st>>>(x, n, amax_bits);
   return check_launch();
 }
 

@@ -316,6 +316,26 @@ __device__ __forceinline__ uint4 ldg16(const void* p) {
                : "l"(p));
   return v;
 }
+// L2 policy that makes lines the first candidates for eviction: for data a
+// kernel touches for the last time, so that it does not displace lines that
+// are about to be read again.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint4 ldg16_last_use(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ void stg8_last_use(void* p, uint32_t a, uint32_t b, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v2.u32 [%0], {%1,%2}, %3;" ::"l"(p),
+               "r"(a), "r"(b), "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ void stg16(void* p, uint4 v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
