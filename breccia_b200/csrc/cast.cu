@@ -514,24 +514,33 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
 
 // --------------------------------------------------------------- 2-D tiles
 // One CTA per (block_m x block_k) tile; the tile's vectors stay in registers
-// between the amax pass and the encode pass.
-template <int DT, int FMT, int MAXV>
+// between the amax pass and the encode pass. VPR > 0 fixes the vectors per
+// tile row at compile time (block_k = 128), so a vector's row and column are
+// a shift and a mask rather than a runtime division.
+template <int DT, int FMT, int MAXV, int VPR>
 __global__ void __launch_bounds__(256) k_block2d_cast(const void* __restrict__ x, int64_t cols,
                                                       int bm, int bk, uint8_t* codes,
                                                       float* scales) {
   constexpr int V = In<DT>::kVec;
   constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
-  const int vec_per_row = bk / V;
+  const int vec_per_row = VPR > 0 ? VPR : bk / V;
   const int nvec = bm * vec_per_row;
   const int64_t r0 = (int64_t)blockIdx.y * bm, c0 = (int64_t)blockIdx.x * bk;
+  // vector idx = threadIdx.x + k * 256 sits at tile row idx / vpr, column
+  // (idx % vpr) * V; with a compile-time vpr dividing 256 the column is fixed
+  // per thread and the row advances by 256 / vpr per k.
+  auto offset = [&](int k) -> int64_t {
+    const int idx = threadIdx.x + k * 256;
+    const int rr = idx / vec_per_row, cc = (idx % vec_per_row) * V;
+    return (r0 + rr) * cols + c0 + cc;
+  };
+  const char* xb = static_cast<const char*>(x);
   uint4 v[MAXV];
   float m = 0.f;
 #pragma unroll
   for (int k = 0; k < MAXV; ++k) {
-    const int idx = threadIdx.x + k * blockDim.x;
-    if (idx < nvec) {
-      const int rr = idx / vec_per_row, cc = (idx % vec_per_row) * V;
-      v[k] = ldg16(static_cast<const char*>(x) + ((r0 + rr) * cols + c0 + cc) * elem_bytes<DT>());
+    if (threadIdx.x + k * 256 < nvec) {
+      v[k] = ldg16(xb + offset(k) * elem_bytes<DT>());
       m = fmax_nan(m, vec_absmax<DT>(v[k]));
     }
   }
@@ -550,28 +559,34 @@ __global__ void __launch_bounds__(256) k_block2d_cast(const void* __restrict__ x
   }
   __syncthreads();
   const float s = s_sh;
-  const bool fast = isfinite(s);
   const float r = __frcp_rn(s);
+  if (isfinite(s)) {
 #pragma unroll
-  for (int k = 0; k < MAXV; ++k) {
-    const int idx = threadIdx.x + k * blockDim.x;
-    if (idx < nvec) {
-      const int rr = idx / vec_per_row, cc = (idx % vec_per_row) * V;
-      float f[V];
-      unpack<DT>(v[k], f);
-      uint32_t w[V / 4];
+    for (int k = 0; k < MAXV; ++k) {
+      if (threadIdx.x + k * 256 < nvec) {
+        float f[V];
+        unpack<DT>(v[k], f);
+        uint32_t w[V / 4];
 #pragma unroll
-      for (int j = 0; j < V / 4; ++j) {
-        if (fast) {
+        for (int j = 0; j < V / 4; ++j)
           w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
                                div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
-        } else {
+        store_words<V / 4>(codes + offset(k), w);
+      }
+    }
+  } else {
+    for (int k = 0; k < MAXV; ++k) {
+      if (threadIdx.x + k * 256 < nvec) {
+        float f[V];
+        unpack<DT>(v[k], f);
+        uint32_t w[V / 4];
+        for (int j = 0; j < V / 4; ++j) {
           uint32_t c = 0;
           for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * j + i], s)) << (8 * i);
           w[j] = c;
         }
+        store_words<V / 4>(codes + offset(k), w);
       }
-      store_words<V / 4>(codes + (r0 + rr) * cols + c0 + cc, w);
     }
   }
 }
@@ -951,7 +966,16 @@ struct Block2d {
     const int64_t nvec = (int64_t)bm * (bk / V);
     if (nvec > 256 * 16) return BRC_ERR_UNSUPPORTED;
     dim3 grid((unsigned)(cols / bk), (unsigned)(rows / bm));
-    k_block2d_cast<DT, FMT, 16><<<grid, 256, 0, st>>>(x, cols, bm, bk, codes, scales);
+    constexpr int kVpr128 = 128 / V;  // vectors per row of a 128-wide tile
+    if (bk == 128) {
+      if (nvec <= 256 * (V == 4 ? 16 : 8))
+        k_block2d_cast<DT, FMT, (V == 4 ? 16 : 8), kVpr128>
+            <<<grid, 256, 0, st>>>(x, cols, bm, bk, codes, scales);
+      else
+        k_block2d_cast<DT, FMT, 16, kVpr128><<<grid, 256, 0, st>>>(x, cols, bm, bk, codes, scales);
+    } else {
+      k_block2d_cast<DT, FMT, 16, 0><<<grid, 256, 0, st>>>(x, cols, bm, bk, codes, scales);
+    }
     return check_launch();
   }
 };
