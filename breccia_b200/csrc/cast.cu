@@ -197,7 +197,15 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
     if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
-    if (a.packed_tiles) store_packed<NW>(a.packed_tiles + tile_off, w);
+    if (a.packed_tiles) {
+      // skinny-GEMM tile order: in each run of 8 elements, byte j holds
+      // element j (low nibble) and element j + 4 (high nibble)
+      static_assert(NW % 2 == 0, "tile packing works on 8-element runs");
+      uint32_t t[NW / 2];
+#pragma unroll
+      for (int i = 0; i < NW / 2; ++i) t[i] = w[2 * i] | (w[2 * i + 1] << 4);
+      store_words<NW / 2>(a.packed_tiles + tile_off, t);
+    }
   }
 }
 
@@ -328,18 +336,21 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
     int64_t tile_off = 0;
     if constexpr (MODE == kInt4Sym || MODE == kInt4Asym) {
       if (a.packed_tiles) {
-        // tile (row / 16, group) of 16 rows x 64 bytes; one fp32 scale / zero
-        // point (the stored value) per tile row
+        // tile (row / 16, group) of 16 rows x 64 bytes; per tile 16 fp32
+        // scales (the stored value) and, asymmetric, 16 fp32 values 128 + the
+        // stored zero point, tile row r at 2 * (r % 8) + r / 8, so that one
+        // 8-byte load gives an MMA thread its rows r and r + 8
         const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
         const uint32_t g = (uint32_t)blk - row * a.blocks_per_row.d;
         const int64_t tile = (int64_t)(row >> 4) * a.blocks_per_row.d + g;
         tile_off = tile * 1024 + (row & 15) * 64 + (part * E) / 2;
         if (part == 0) {
+          const int64_t q = tile * 16 + (row & 7) * 2 + ((row >> 3) & 1);
           const float sv = a.scale_f16 ? __half2float(to_half_canon(s)) : canon_nan(s);
-          a.scale_tiles[tile * 16 + (row & 15)] = sv;
+          a.scale_tiles[q] = sv;
           if constexpr (MODE == kInt4Asym) {
             const float zv = a.scale_f16 ? __half2float(to_half_canon(zp)) : canon_nan(zp);
-            a.zp_tiles[tile * 16 + (row & 15)] = zv;
+            a.zp_tiles[q] = __fadd_rn(128.f, zv);
           }
         }
       }

@@ -146,11 +146,14 @@ int brc_cast_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t cols, uint8
  * codes (optional): one code per byte (low nibble). packed (optional): two
  * per byte, element 2i in the LOW nibble.
  * packed_tiles / scale_tiles / zp_tiles (optional; group == 128 and
- * rows % 16 == 0): the layout brc_gemm_int4 streams. Tile (r/16, g) of
- * 16 rows x 128 elements is 1024 bytes at ((r/16) * (cols/128) + g) * 1024,
- * row r%16 at +64*(r%16), codes packed as above; scale_tiles / zp_tiles hold
- * the stored scale / zero point as float32 at ((r/16) * (cols/128) + g) * 16
- * + r%16. zp_tiles is required iff !symmetric.
+ * rows % 16 == 0): the layout brc_gemm_int4 streams. Tile T = (r/16) *
+ * (cols/128) + g covers rows r/16*16 .. +15 and group g: 1024 bytes at
+ * T * 1024, row r%16 at +64*(r%16); in each run of 8 elements 8j .. 8j+7 of
+ * the row's group, byte 4j + i holds element 8j + i in the low nibble and
+ * element 8j + i + 4 in the high nibble (i < 4). scale_tiles holds the
+ * stored scale as float32 and zp_tiles (asymmetric only, else ignored)
+ * 128 + the stored zero point as float32, both at T * 16 + 2 * (r%8) +
+ * (r%16)/8.
  */
 int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int group,
                   int is_signed, int symmetric, int scale_dtype, uint8_t* codes,

@@ -233,6 +233,37 @@ def test_packed_side_outputs():
         np.testing.assert_array_equal(mma[off], sf)
 
 
+@pytest.mark.parametrize("symmetric", [False, True])
+def test_int4_gemm_tile_layout(symmetric):
+    """INT4 skinny-GEMM tiles: tile T = (r // 16) * (cols // 128) + g of 1 KB,
+    row r % 16 at 64 * (r % 16); in each run of 8 elements 8j..8j+7 byte
+    4j + i holds element 8j + i (low nibble) and 8j + i + 4 (high nibble);
+    scale / 128 + zero point at T * 16 + 2 * (r % 8) + (r % 16) // 8."""
+    from breccia_b200.types import INT4Scaling
+    rows, cols = 48, 384
+    r = INT4Scaling(group_size=128, signed=False, symmetric=symmetric)
+    x = (torch.randn(rows, cols) * 0.02).cuda()
+    st = bb().cast(x, r)
+    side = bb().gemm_operands(st)
+    codes = st.data.cpu().numpy().astype(np.uint8)
+    groups = cols // 128
+    rr, cc = np.meshgrid(np.arange(rows), np.arange(cols), indexing="ij")
+    g, e = cc // 128, cc % 128
+    tile = (rr // 16) * groups + g
+    byte = tile * 1024 + (rr % 16) * 64 + (e // 8) * 4 + (e % 4)
+    high = (e % 8) >= 4
+    tiles = side["int4_tiles"].cpu().numpy()
+    got = np.where(high, tiles[byte] >> 4, tiles[byte] & 0xF)
+    np.testing.assert_array_equal(got, codes)
+    rrs, gs = np.meshgrid(np.arange(rows), np.arange(groups), indexing="ij")
+    q = ((rrs // 16) * groups + gs) * 16 + 2 * (rrs % 8) + (rrs % 16) // 8
+    np.testing.assert_array_equal(side["int4_scale_tiles"].cpu().numpy()[q],
+                                  st.scale.float().cpu().numpy())
+    if not symmetric:
+        np.testing.assert_array_equal(side["int4_zp_tiles"].cpu().numpy()[q],
+                                      128.0 + st.zero_point.float().cpu().numpy())
+
+
 def test_division_matches_ieee():
     from breccia_b200 import _lib
     g = torch.Generator().manual_seed(5)

@@ -222,6 +222,26 @@ def test_int4_weight_only(M, variant):
     _check(out.cpu().numpy(), ref, tight=1e-4)
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 16 * 149, 5120), (3, 16 * 300, 3072), (9, 16 * 7, 1024),
+                                   (1, 16, 1024), (16, 16 * 2, 8192)])
+def test_int4_weight_only_shapes(M, N, K):
+    """Ragged work splits of the skinny GEMM: more row blocks than SMs, fewer
+    row blocks than warps, one row block, activations streamed in an odd
+    number of double-buffered chunks (M = 16, K = 5120), asymmetric g128."""
+    from oracle import cast as ocast
+    from breccia_b200.types import INT4Scaling
+    r = INT4Scaling(group_size=128, signed=False, symmetric=False)
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    Wt = torch.randn(N, K, generator=g) * 0.02
+    sw = bb().cast(Wt.cuda(), r)
+    out = bb().linear(A.cuda(), sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    qw = ocast.cast(Wt.numpy(), r)
+    ref = ocast.matmul(A.float().numpy(), ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-4)
+
+
 def test_int4_weight_only_config5_shape():
     """W^T (28672, 8192) f32 ~ N(0, 0.02), asymmetric g128,
     activations (16, 8192) bf16; checked on a column sample of the output."""
