@@ -14,11 +14,16 @@
 // keep the per-element instruction count low enough (~10-14 ops) that a
 // 2-byte input stays bandwidth-bound.
 
+#include <mutex>
+
 #include "common.cuh"
 #include "e8m0_thresholds.h"
 #include "launch.h"
+#include "sm100.cuh"
 
 namespace brc {
+
+uint32_t* gemm_status_ptr();  // device address of the status word (gemm_sm100.cu)
 
 __device__ const uint32_t g_e8m0_thr[kE8m0Binades] = {BRC_E8M0_THRESHOLDS};
 
@@ -602,6 +607,133 @@ __global__ void __launch_bounds__(256) k_block2d_cast(const void* __restrict__ x
   }
 }
 
+// Persistent, TMA-fed form for 128-wide tiles: each (bm x 128) tile arrives
+// in one 2-D tensor copy into a ring of shared-memory stages; the threads copy
+// it into registers, the stage is refilled at once, and the tile's amax
+// reduction and encode run from registers while the next tiles stream in.
+// Every wait is bounded; a timeout is decided for the whole CTA through
+// __syncthreads_or, the status word records it and the CTA stops after
+// waiting for its own copies in flight.
+constexpr int kB2dThreads = 512;
+
+template <int DT, int FMT, int NV>  // NV = 16-byte vectors per thread per tile (bm <= 128)
+__global__ void __launch_bounds__(kB2dThreads, 1)
+    k_block2d_cast_tma(const __grid_constant__ CUtensorMap tm, int64_t rows, int64_t cols, int bm,
+                       int stages, uint8_t* codes, float* scales, uint32_t* status) {
+  using namespace sm100;
+  constexpr int V = In<DT>::kVec;
+  constexpr int VPR = 128 / V;  // vectors per tile row
+  constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tile_bytes = bm * 128 * elem_bytes<DT>();
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)stages * tile_bytes);
+  float* red = reinterpret_cast<float*>(full + stages);  // one value per warp
+  float* s_sh = red + kB2dThreads / 32;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(s_sh + 1);
+  const int64_t tiles_c = cols / 128;
+  const int64_t ntiles = tiles_c * (rows / bm);
+  const int nvec = bm * VPR;
+  const int64_t my_tiles =
+      ntiles > (int64_t)blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int64_t issued = 0;  // thread 0: tiles whose copy has been issued
+  auto issue = [&]() {
+    const int64_t t = blockIdx.x + issued * gridDim.x;
+    const int s = (int)(issued % stages);
+    mbar_arrive_expect_tx(&full[s], (uint32_t)tile_bytes);
+    tma_load_2d(smem + (size_t)s * tile_bytes, &tm, (int32_t)((t % tiles_c) * 128),
+                (int32_t)((t / tiles_c) * bm), &full[s]);
+    ++issued;
+  };
+  if (threadIdx.x == 0)
+    while (issued < stages && issued < my_tiles) issue();
+
+  bool aborted = false;
+  for (int64_t j = 0; j < my_tiles; ++j) {
+    const int s = (int)(j % stages);
+    const bool ok = mbar_wait(&full[s], (uint32_t)((j / stages) & 1), abort_flag, status, 1u);
+    uint4 v[NV];
+    float m = 0.f;
+    if (ok) {
+      const uint8_t* tile = smem + (size_t)s * tile_bytes;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int idx = threadIdx.x + k * kB2dThreads;
+        if (idx < nvec) {
+          v[k] = *reinterpret_cast<const uint4*>(tile + (size_t)idx * 16);
+          m = fmax_nan(m, vec_absmax<DT>(v[k]));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    if (__syncthreads_or(!ok)) {  // also: every thread has read stage s
+      aborted = true;
+      break;
+    }
+    const int64_t t = blockIdx.x + j * gridDim.x;
+    if (threadIdx.x == 0) {
+      if (issued < my_tiles && !*abort_flag) issue();
+      float a = red[0];
+      for (int w = 1; w < kB2dThreads / 32; ++w) a = fmax_nan(a, red[w]);
+      const float sc = __fdiv_rn(fmax_nan(a, 1e-10f), kMax);
+      *s_sh = sc;
+      scales[t] = canon_nan(sc);
+    }
+    __syncthreads();
+    const float sc = *s_sh;
+    const float r = __frcp_rn(sc);
+    uint8_t* cbase = codes + (t / tiles_c) * bm * cols + (t % tiles_c) * 128;
+    if (isfinite(sc)) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int idx = threadIdx.x + k * kB2dThreads;
+        if (idx < nvec) {
+          float f[V];
+          unpack<DT>(v[k], f);
+          uint32_t w[V / 4];
+#pragma unroll
+          for (int q = 0; q < V / 4; ++q)
+            w[q] = enc4_fp8<FMT>(div_by(f[4 * q], sc, r), div_by(f[4 * q + 1], sc, r),
+                                 div_by(f[4 * q + 2], sc, r), div_by(f[4 * q + 3], sc, r));
+          store_words<V / 4>(cbase + (int64_t)(idx / VPR) * cols + (idx % VPR) * V, w);
+        }
+      }
+    } else {
+      for (int k = 0; k < NV; ++k) {
+        const int idx = threadIdx.x + k * kB2dThreads;
+        if (idx < nvec) {
+          float f[V];
+          unpack<DT>(v[k], f);
+          uint32_t w[V / 4];
+          for (int q = 0; q < V / 4; ++q) {
+            uint32_t c = 0;
+            for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * q + i], sc)) << (8 * i);
+            w[q] = c;
+          }
+          store_words<V / 4>(cbase + (int64_t)(idx / VPR) * cols + (idx % VPR) * V, w);
+        }
+      }
+    }
+  }
+  if (aborted && threadIdx.x == 0) {
+    // wait (bounded) for the copies still in flight before the CTA exits
+    for (int64_t q = issued > stages ? issued - stages : 0; q < issued; ++q) {
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(&full[q % stages], (uint32_t)((q / stages) & 1)) &&
+             globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  }
+}
+
 // --------------------------------------------------------------- dequantize
 // 16 codes per lane-iteration; out = decode(code) * scale.
 enum DqMode { kDqFp8 = 0, kDqMx = 1, kDqNv = 2, kDqInt4 = 3 };
@@ -976,6 +1108,38 @@ struct Block2d {
     if (bk % V) return BRC_ERR_UNSUPPORTED;
     const int64_t nvec = (int64_t)bm * (bk / V);
     if (nvec > 256 * 16) return BRC_ERR_UNSUPPORTED;
+    if (bk == 128 && bm <= 128 && (cols * elem_bytes<DT>()) % 16 == 0 &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      // persistent TMA-fed form
+      constexpr int NV = (128 * (128 / V) + kB2dThreads - 1) / kB2dThreads;
+      auto kern = k_block2d_cast_tma<DT, FMT, NV>;
+      static std::once_flag once[64];
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BRC_ERR_CUDA;
+      constexpr int kSmemMax = 227 * 1024;
+      std::call_once(once[dev], [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+      });
+      const int tile_bytes = bm * 128 * elem_bytes<DT>();
+      const int extra = 16 * 8 + (kB2dThreads / 32 + 1) * 4 + 16;
+      int stages = (kSmemMax - extra) / tile_bytes;
+      if (stages > 6) stages = 6;
+      if (stages >= 2) {
+        CUtensorMap tm;
+        const CUtensorMapDataType dt = DT == BRC_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : DT == BRC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        int rc = encode_tmap_2d(&tm, dt, x, (uint64_t)cols, (uint64_t)rows,
+                                (uint64_t)cols * elem_bytes<DT>(), 128, (uint32_t)bm);
+        if (rc) return rc;
+        const int64_t ntiles = (cols / 128) * (rows / bm);
+        const int grid = (int)(ntiles < sm_count() ? ntiles : sm_count());
+        const size_t smem = (size_t)stages * tile_bytes + extra;
+        kern<<<grid, kB2dThreads, smem, st>>>(tm, rows, cols, bm, stages, codes, scales,
+                                               gemm_status_ptr());
+        return check_launch();
+      }
+    }
     dim3 grid((unsigned)(cols / bk), (unsigned)(rows / bm));
     constexpr int kVpr128 = 128 / V;  // vectors per row of a 128-wide tile
     if (bk == 128) {

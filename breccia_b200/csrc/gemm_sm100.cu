@@ -672,6 +672,20 @@ Params base_params(int M, int N, int K, int k_per_stage, void* d) {
 }  // namespace brc
 
 namespace brc {
+int encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                   uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  gemm::EncodeTiledFn fn = gemm::encode_fn();
+  if (!fn) return BRC_ERR_CUDA;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BRC_OK : BRC_ERR_CUDA;
+}
+
 // Device address of the sticky GEMM status word, for kernels in other
 // translation units. Looked up once per device (with that device current) and
 // cached, so later launches make no runtime lookups.

@@ -233,6 +233,33 @@ def test_packed_side_outputs():
         np.testing.assert_array_equal(mma[off], sf)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("fmt", ["E4M3", "E5M2"])
+@pytest.mark.parametrize("block_m,rows,cols", [(128, 384, 640), (64, 192, 384), (32, 96, 256),
+                                              (128, 128 * 20, 128 * 9)])
+def test_block2d_vs_oracle(dtype, fmt, block_m, rows, cols):
+    """128 x 128 (and 64 / 32 x 128) weight-tile cast, bit-exact against the
+    restated oracle; one tile holds a NaN, one an inf, one is all zeros and
+    one sits below the 1e-10 amax floor. The last shape has more tiles than
+    SMs (the persistent form's grid-stride loop)."""
+    from oracle import cast as ocast
+    from breccia_b200.types import Float8BlockScaling
+    r = Float8BlockScaling(fp8_format=fmt)
+    g = torch.Generator().manual_seed(rows + cols + block_m)
+    x = torch.randn(rows, cols, generator=g) * torch.exp2(torch.randint(-6, 6, (rows, 1),
+                                                                         generator=g).float())
+    x[1, 3] = float("nan")
+    x[block_m + 2, 128 + 5] = float("inf")
+    x[:block_m, 256:384] = 0.0
+    x[block_m:2 * block_m, 0:128] *= 1e-30
+    x = x.to(dtype)
+    st = bb().cast(x.cuda(), r, block_m=block_m)
+    torch.cuda.synchronize()
+    q = ocast.cast_block_fp8_2d(x.float().numpy(), r, block_m=block_m)
+    np.testing.assert_array_equal(st.data.view(torch.uint8).cpu().numpy(), q.data)
+    assert same_bits(st.scale.cpu().numpy(), q.scale)
+
+
 @pytest.mark.parametrize("symmetric", [False, True])
 def test_int4_gemm_tile_layout(symmetric):
     """INT4 skinny-GEMM tiles: tile T = (r // 16) * (cols // 128) + g of 1 KB,
