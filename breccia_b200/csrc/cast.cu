@@ -181,24 +181,38 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
     // 1.5 * 2^23 addition; the low nibble of the sum's bits is the code.
     const float lo = (MODE == kInt4Sym && a.is_signed) ? -8.f : 0.f;
     const float hi = (MODE == kInt4Sym && a.is_signed) ? 7.f : 15.f;
-    const float r = fast ? __frcp_rn(s) : 0.f;
+    if (fast) {
+      const float r = __frcp_rn(s);
 #pragma unroll
-    for (int j = 0; j < NW; ++j) {
-      uint32_t c = 0;
+      for (int j = 0; j < NW; ++j) {
+        uint32_t c = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float q = fast ? div_by(f[4 * j + i], s, r) : div_ieee(f[4 * j + i], s);
-        if constexpr (MODE == kInt4Asym) q = __fadd_rn(q, zp);
-        uint32_t code;
-        if (!fast && isnan(q)) {
-          code = 0u;  // NumPy's float->uint8 conversion of NaN gives 0
-        } else {
+        for (int i = 0; i < 4; ++i) {
+          float q = div_by(f[4 * j + i], s, r);
+          if constexpr (MODE == kInt4Asym) q = __fadd_rn(q, zp);
+          // np.round(np.clip(q, lo, hi)) with half-to-even rounding via
+          // 1.5 * 2^23; NaN inputs clip to lo with fminf/fmaxf, but a block
+          // holding a NaN has a NaN statistic and takes the slow path
           const float v = fminf(fmaxf(q, lo), hi);
-          code = __float_as_uint(__fadd_rn(v, 12582912.f)) & 0xFu;
+          c |= (__float_as_uint(__fadd_rn(v, 12582912.f)) & 0xFu) << (8 * i);
         }
-        c |= code << (8 * i);
+        w[j] = c;
       }
-      w[j] = c;
+    } else {
+      for (int j = 0; j < NW; ++j) {
+        uint32_t c = 0;
+        for (int i = 0; i < 4; ++i) {
+          float q = div_ieee(f[4 * j + i], s);
+          if constexpr (MODE == kInt4Asym) q = __fadd_rn(q, zp);
+          uint32_t code = 0u;  // NumPy's float->uint8 conversion of NaN gives 0
+          if (!isnan(q)) {
+            const float v = fminf(fmaxf(q, lo), hi);
+            code = __float_as_uint(__fadd_rn(v, 12582912.f)) & 0xFu;
+          }
+          c |= code << (8 * i);
+        }
+        w[j] = c;
+      }
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
     if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
@@ -280,13 +294,14 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
     bool fast;
     if constexpr (MODE == kBlockFp8) {
       constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
-      s = __fdiv_rn(fmax_nan(st0, 1e-10f), kMax);
+      s = div_const(fmax_nan(st0, 1e-10f), kMax, FMT == BRC_FP8_E4M3 ? kRcp448 : kRcp57344);
       if (part == 0) static_cast<float*>(a.scales)[blk] = canon_nan(s);
       fast = isfinite(s);
     } else if constexpr (MODE == kMxfp8) {
       constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
       const float am = fmax_nan(st0, 1e-10f);
-      const uint32_t e = e8m0_code(__fdiv_rn(am, kMax), g_e8m0_thr);
+      const uint32_t e =
+          e8m0_code(div_const(am, kMax, FMT == BRC_FP8_E4M3 ? kRcp448 : kRcp57344), g_e8m0_thr);
       if (part == 0) {
         static_cast<uint8_t*>(a.scales)[blk] = (uint8_t)e;
         if (a.scales_mma) {
@@ -301,7 +316,7 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
                : (e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127));
     } else if constexpr (MODE == kNvfp4) {
       const float am = fmax_nan(st0, 1e-10f);
-      const uint32_t sc = enc1_e4m3(__fdiv_rn(am, 6.f));
+      const uint32_t sc = enc1_e4m3(div_const(am, 6.f, kRcp6));
       float actual = dec_e4m3(sc);
       if (!(actual > 0.f)) actual = 0x1p-9f;  // np.where(actual > 0, actual, 2^-9)
       if (part == 0) {
@@ -315,7 +330,8 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       s = actual;
       fast = isfinite(am);
     } else if constexpr (MODE == kInt4Sym) {
-      s = __fdiv_rn(fmax_nan(st0, 1e-10f), a.is_signed ? 7.f : 15.f);
+      s = a.is_signed ? div_const(fmax_nan(st0, 1e-10f), 7.f, kRcp7)
+                      : div_const(fmax_nan(st0, 1e-10f), 15.f, kRcp15);
       if (part == 0) {
         if (a.scale_f16) static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
         else static_cast<float*>(a.scales)[blk] = canon_nan(s);
@@ -323,7 +339,7 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       fast = isfinite(s);
     } else {
       const float range = fmax_nan(__fsub_rn(st1, st0), 1e-10f);
-      s = __fdiv_rn(range, 15.f);
+      s = div_const(range, 15.f, kRcp15);
       const float zf = rintf(__fdiv_rn(-st0, s));
       // np.clip keeps the operand (including -0.0 and NaN) when it is in range
       zp = zf < 0.f ? 0.f : (zf > 15.f ? 15.f : zf);
@@ -950,13 +966,14 @@ int dispatch_dt_fmt(int dt, int fmt, Args... args) {
 }
 
 // Launch the vectorised block kernel for block size B with LPB lanes per
-// block, choosing LPB so each lane owns 32 bytes (16 halves / 8 floats) or,
-// for big blocks, 64 bytes.
+// block, choosing LPB so each lane owns 64 bytes (32 halves / 16 floats), or
+// the whole block when it is smaller. The per-block work (statistic, scale,
+// scale stores) then runs on as few lanes as possible.
 template <int DT, int MODE, int FMT, int B>
 int launch_block_b(const BlockCastArgs& a, cudaStream_t st) {
   constexpr int V = In<DT>::kVec;
-  constexpr int E0 = (DT == BRC_DTYPE_F32) ? 8 : 16;  // 32 bytes per lane
-  constexpr int E = (B >= 128) ? 2 * E0 : (B < E0 ? B : E0);
+  constexpr int E0 = (DT == BRC_DTYPE_F32) ? 16 : 32;  // 64 bytes per lane
+  constexpr int E = B < E0 ? B : E0;
   constexpr int LPB = B / E;
   static_assert(E % V == 0 && LPB >= 1 && LPB <= 32, "bad lane split");
   const int64_t tiles = (a.n_blocks + (32 / LPB) - 1) / (32 / LPB);

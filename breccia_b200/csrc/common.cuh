@@ -129,6 +129,18 @@ __device__ __forceinline__ float div_by(float x, float s, float r) {
 }
 __device__ __forceinline__ float div_ieee(float x, float s) { return __fdiv_rn(x, s); }
 
+// IEEE x / d for a constant d with rd = RN(1/d): Markstein's step for finite
+// x (the callers' x are amax values floored at 1e-10, so the quotient is a
+// normal float), the division itself for inf and NaN.
+constexpr float kRcp448 = 0x1.24924ap-9f;    // RN(1/448), bits 0x3B124925
+constexpr float kRcp57344 = 0x1.24924ap-16f; // RN(1/57344), bits 0x37924925
+constexpr float kRcp6 = 0x1.555556p-3f;      // RN(1/6), bits 0x3E2AAAAB
+constexpr float kRcp7 = 0x1.24924ap-3f;      // RN(1/7), bits 0x3E124925
+constexpr float kRcp15 = 0x1.111112p-4f;     // RN(1/15), bits 0x3D888889
+__device__ __forceinline__ float div_const(float x, float d, float rd) {
+  return isfinite(x) ? div_by(x, d, rd) : __fdiv_rn(x, d);
+}
+
 // ------------------------------------------------------------ FP8 / FP4 encode
 // Magnitude encoders. The float is first scaled by a power of two that puts
 // the format's smallest normal at float32's smallest normal (2^-126), with
