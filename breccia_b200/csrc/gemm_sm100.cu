@@ -351,6 +351,208 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA pairs
+// Per-tensor FP8 GEMM on CTA pairs (tcgen05 cta_group::2). A cluster of two
+// CTAs on a pair of SMs computes a 256 x 256 tile: each CTA loads its 128
+// rows of A and 128 rows of B^T (its half of the tile's N) into its own
+// shared memory, so a stage is 32 KB per CTA and the ring is 6 deep (the
+// single-CTA kernel moves 48 KB per stage through a 4-deep ring). Both CTAs'
+// copies complete on the leader's (rank 0's) "full" barrier, the leader's
+// single MMA thread issues M = 256 MMAs, and their commits reach both CTAs'
+// "empty" and accumulator barriers; both CTAs' epilogue warps release the
+// accumulator on the leader's barrier. A cluster barrier brackets set-up and
+// tear-down so no CTA leaves while its partner may still signal it.
+constexpr int P_STAGES = 6;
+constexpr int P_BM = 256, P_BN = 256;
+constexpr uint32_t P_A_BYTES = 128 * BKB;  // this CTA's 128 rows of A
+constexpr uint32_t P_B_BYTES = 128 * BKB;  // this CTA's 128 rows of B^T
+struct SmemPair {
+  static constexpr uint32_t kA = 0;
+  static constexpr uint32_t kB = kA + P_STAGES * P_A_BYTES;
+  static constexpr uint32_t kBar = kB + P_STAGES * P_B_BYTES;
+  static constexpr uint32_t kNumBars = 2 * P_STAGES + 3;  // full, empty, acc full/empty, drain
+  static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
+  static constexpr uint32_t kTotal = kMisc + 16;
+  static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
+};
+
+template <int AFMT, int BFMT, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmap_a,
+                const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  using L = SmemPair;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tmem_full = empty + P_STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain = tmem_empty + 1;
+  uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int num_tiles = p.num_m * p.num_n;  // 256 x 256 tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 2 * kEpiWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_sh, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_sh;
+  const uint32_t full_leader = mapa_shared(smem_u32(full), 0u);
+  const uint32_t tmem_empty_leader = mapa_shared(smem_u32(tmem_empty), 0u);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;  // per-stage bits for the drain
+      bool ok = true;
+      for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          // the leader expects both CTAs' bytes on its own barrier
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
+          const uint32_t fb = full_leader + 8u * stage;
+          tma_load_2d_pair(smem + L::kA + stage * P_A_BYTES, &tmap_a, kb * BKB,
+                           mb * P_BM + 128 * (int)rank, fb);
+          tma_load_2d_pair(smem + L::kB + stage * P_B_BYTES, &tmap_b, kb * BKB,
+                           nb * P_BN + 128 * (int)rank, fb);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // the leader's barriers count both CTAs' copies: wait (bounded) for
+        // those in flight before the pair leaves
+        for (int s = 0; s < P_STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t idesc = idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN);
+      for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, abort_flag, p.status, 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kA + stage * P_A_BYTES);
+          const uint32_t b_addr = smem_u32(smem + L::kB + stage * P_B_BYTES);
+#pragma unroll
+          for (uint32_t k = 0; k < 4; ++k)
+            mma_f8f6f4_pair(tmem + ACC_COL, desc_kmajor_sw128(a_addr + 32 * k),
+                            desc_kmajor_sw128(b_addr + 32 * k), idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(tmem_full, 0x3);
+        acc_phase ^= 1u;
+      }
+      // every MMA issued has completed before the pair frees TMEM
+      tc_commit_pair(drain, 0x1);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int half = ew / 4;    // which 128 accumulator columns
+    const float scale = __fmul_rn(*p.a_scale, *p.b_scale);
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      if (!mbar_wait(tmem_full, acc_phase, abort_flag, p.status, 1u)) break;
+      acc_phase ^= 1u;
+      tc_fence_after();
+      uint32_t r[4][32];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + ACC_COL + 128 * half;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tmem_empty_leader);
+      const int row = mb * P_BM + 128 * (int)rank + 32 * quad + lane;
+      const int col0 = nb * P_BN + 128 * half;
+      if (row < p.M) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__uint_as_float(r[c][i]), scale);
+          store_row_chunk<OUT>(p.d, p.ldd, row, col0 + 32 * c, p.N, v, 32);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ block FP8
 // DeepSeek-v3 style Float8BlockScaling: A with 1 x 128 float32 scales, B with
 // 128 x 128 float32 scales. Float32 (non power of two) scales cannot ride in
@@ -597,6 +799,34 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
   return check_launch();
 }
 
+template <int AFMT, int BFMT, int OUT>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  auto kern = k_gemm_pair<AFMT, BFMT, OUT>;
+  const int smem = (int)SmemPair::kAlloc;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return BRC_ERR_CUDA;
+  if (!configured[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (rc) return rc;
+    configured[dev] = true;
+  }
+  const int tiles = p.num_m * p.num_n;
+  const int pairs = sm_count() / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return check_launch();
+}
+
+template <int AFMT, int BFMT>
+int launch_pair_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                    cudaStream_t st) {
+  if (out_dtype == BRC_DTYPE_F32) return launch_pair<AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, p, st);
+  if (out_dtype == BRC_DTYPE_BF16) return launch_pair<AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, p, st);
+  return launch_pair<AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, p, st);
+}
+
 template <int KIND, int AFMT, int BFMT>
 int launch_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                cudaStream_t st) {
@@ -725,14 +955,32 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
     return BRC_ERR_DTYPE;
   if ((int64_t)M * N == 0) return BRC_OK;
   if (K == 0) return BRC_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
   CUtensorMap ta, tb;
+  // CTA pairs (256 x 256 tiles) when they fill the GPU, single CTAs else
+  const int pair_tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  if (pair_tiles >= sm_count() / 2) {
+    if ((rc = make_tmap(&ta, a, M, K, 128))) return rc;
+    if ((rc = make_tmap(&tb, b, N, K, 128))) return rc;
+    Params p = base_params(M, N, K, BKB, d);
+    p.num_m = (M + P_BM - 1) / P_BM;
+    p.num_n = (N + P_BN - 1) / P_BN;
+    p.group_m = kGroupM / 2;  // the same 2048 rows of A per tile group
+    p.a_scale = a_scale;
+    p.b_scale = b_scale;
+    p.status = status_word();
+    if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<0, 0>(d_dtype, ta, tb, p, st);
+    if (a_fmt == BRC_FP8_E4M3) return launch_pair_out<0, 1>(d_dtype, ta, tb, p, st);
+    if (b_fmt == BRC_FP8_E4M3) return launch_pair_out<1, 0>(d_dtype, ta, tb, p, st);
+    return launch_pair_out<1, 1>(d_dtype, ta, tb, p, st);
+  }
   if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
   if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
   Params p = base_params(M, N, K, BKB, d);
   p.a_scale = a_scale;
   p.b_scale = b_scale;
   p.status = status_word();
-  cudaStream_t st = (cudaStream_t)stream;
   if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
     return launch_out<kPerTensor, 0, 0>(d_dtype, ta, tb, p, st);
   if (a_fmt == BRC_FP8_E4M3) return launch_out<kPerTensor, 0, 1>(d_dtype, ta, tb, p, st);

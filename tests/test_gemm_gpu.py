@@ -104,6 +104,23 @@ def test_linear_vs_oracle(kind, M, N, K):
     _check(out.cpu().numpy(), ref, tight=1e-5)
 
 
+@pytest.mark.parametrize("kind", ["current", "delayed_e5m2"])
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 512), (2000, 2576, 384), (4096, 4864, 256)])
+def test_per_tensor_cta_pair_path(kind, M, N, K):
+    """Shapes large enough for the CTA-pair GEMM (256 x 256 tiles, at least
+    one per SM pair): ragged M and N, several tiles per pair."""
+    from oracle import cast as ocast
+    r = _recipe(kind)
+    A, W = _operands(M, N, K, seed=M + N + K + 7)
+    sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
+    out = bb().linear(sa, sw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _gemm_status() == 0
+    qa, qw = ocast.cast(A.float().numpy(), r), ocast.cast(W.float().numpy(), r)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    _check(out.cpu().numpy(), ref, tight=1e-5)
+
+
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("kind", ["current", "mxfp8", "nvfp4"])
 def test_output_dtypes(kind, out_dtype):
