@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // "empty" and accumulator barriers; both CTAs' epilogue warps release the
 // accumulator on the leader's barrier. A cluster barrier brackets set-up and
 // tear-down so no CTA leaves while its partner may still signal it.
-constexpr int P_STAGES = 6;
+constexpr int P_STAGES = 7;
 constexpr int P_BM = 256, P_BN = 256;
 constexpr uint32_t P_A_BYTES = 128 * BKB;  // this CTA's 128 rows of A
 constexpr uint32_t P_B_BYTES = 128 * BKB;  // this CTA's 128 rows of B^T
@@ -370,7 +370,7 @@ struct SmemPair {
   static constexpr uint32_t kA = 0;
   static constexpr uint32_t kB = kA + P_STAGES * P_A_BYTES;
   static constexpr uint32_t kBar = kB + P_STAGES * P_B_BYTES;
-  static constexpr uint32_t kNumBars = 2 * P_STAGES + 3;  // full, empty, acc full/empty, drain
+  static constexpr uint32_t kNumBars = 2 * P_STAGES + 5;  // full, empty, 2 x acc full/empty, drain
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
@@ -386,9 +386,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* empty = full + P_STAGES;
-  uint64_t* tmem_full = empty + P_STAGES;
-  uint64_t* tmem_empty = tmem_full + 1;
-  uint64_t* drain = tmem_empty + 1;
+  uint64_t* tmem_full = empty + P_STAGES;  // two accumulator buffers of 256 columns
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* drain = tmem_empty + 2;
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
 
@@ -403,8 +403,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, 2 * kEpiWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 2 * kEpiWarps);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0u;
     fence_mbar_init();
@@ -470,16 +472,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (rank == 0 && lane == 0) {
-      int stage = 0;
+      int stage = 0, abuf = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t idesc = idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN);
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
-        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, abort_flag, p.status, 1u)) {
+        // accumulator buffer abuf: free once both CTAs' epilogues read it
+        if (!mbar_wait(&tmem_empty[abuf], acc_phase ^ 1u, abort_flag, p.status, 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t dacc = tmem + 256u * abuf;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
             ok = false;
@@ -490,7 +494,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = smem_u32(smem + L::kB + stage * P_B_BYTES);
 #pragma unroll
           for (uint32_t k = 0; k < 4; ++k)
-            mma_f8f6f4_pair(tmem + ACC_COL, desc_kmajor_sw128(a_addr + 32 * k),
+            mma_f8f6f4_pair(dacc, desc_kmajor_sw128(a_addr + 32 * k),
                             desc_kmajor_sw128(b_addr + 32 * k), idesc,
                             (kb > 0 || k > 0) ? 1u : 0u);
           tc_commit_pair(&empty[stage], 0x3);
@@ -500,8 +504,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        tc_commit_pair(tmem_full, 0x3);
-        acc_phase ^= 1u;
+        tc_commit_pair(&tmem_full[abuf], 0x3);
+        if (++abuf == 2) {
+          abuf = 0;
+          acc_phase ^= 1u;
+        }
       }
       // every MMA issued has completed before the pair frees TMEM
       tc_commit_pair(drain, 0x1);
@@ -516,20 +523,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = ew / 4;    // which 128 accumulator columns
     const float scale = __fmul_rn(*p.a_scale, *p.b_scale);
     uint32_t acc_phase = 0;
+    int abuf = 0;
     for (int tile = cluster; tile < num_tiles; tile += nclusters) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
-      if (!mbar_wait(tmem_full, acc_phase, abort_flag, p.status, 1u)) break;
-      acc_phase ^= 1u;
+      if (!mbar_wait(&tmem_full[abuf], acc_phase, abort_flag, p.status, 1u)) break;
       tc_fence_after();
       uint32_t r[4][32];
-      const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + ACC_COL + 128 * half;
+      const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + 256u * abuf + 128 * half;
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, r[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tmem_empty_leader);
+      if (lane == 0) mbar_arrive_cluster(tmem_empty_leader + 8u * abuf);
+      if (++abuf == 2) {
+        abuf = 0;
+        acc_phase ^= 1u;
+      }
       const int row = mb * P_BM + 128 * (int)rank + 32 * quad + lane;
       const int col0 = nb * P_BN + 128 * half;
       if (row < p.M) {
