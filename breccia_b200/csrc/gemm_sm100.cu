@@ -53,6 +53,13 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t A_BYTES = BM * BKB;  // 16 KB
 constexpr uint32_t B_BYTES = BN * BKB;  // 32 KB
+// Tiles are visited in groups of kGroupM row blocks, row block fastest: the
+// CTAs in flight share kGroupM A panels (BM x K) and about 148 / kGroupM B
+// panels (BN x K); A is read from DRAM about once and B about num_m / kGroupM
+// times (C2, 16384 x 8192 x 8192: 664 MB read per launch). Measured on B200:
+// 32 raised the reads to 1.5 GB and slowed the MXFP8 GEMM of 8192 x 28672 x
+// 8192 from 1.63 to 2.18 ms; 4 and 8 were 3-15% slower than 16.
+constexpr int kGroupM = 16;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;
 constexpr uint32_t SF_COL = 256;
@@ -352,45 +359,67 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ CTA pairs
-// Per-tensor FP8 GEMM on CTA pairs (tcgen05 cta_group::2). A cluster of two
-// CTAs on a pair of SMs computes a 256 x 256 tile: each CTA loads its 128
-// rows of A and 128 rows of B^T (its half of the tile's N) into its own
-// shared memory, so a stage is 32 KB per CTA and the ring is 6 deep (the
-// single-CTA kernel moves 48 KB per stage through a 4-deep ring). Both CTAs'
-// copies complete on the leader's (rank 0's) "full" barrier, the leader's
-// single MMA thread issues M = 256 MMAs, and their commits reach both CTAs'
-// "empty" and accumulator barriers; both CTAs' epilogue warps release the
-// accumulator on the leader's barrier. A cluster barrier brackets set-up and
-// tear-down so no CTA leaves while its partner may still signal it.
-constexpr int P_STAGES = 7;
+// GEMMs on CTA pairs (tcgen05 cta_group::2). A cluster of two CTAs on a pair
+// of SMs computes a 256 x 256 tile: each CTA loads its 128 rows of A and 128
+// rows of B^T (its half of the tile's N) into its own shared memory, so a
+// stage is ~32 KB per CTA and the ring is 5-7 deep (the single-CTA kernel
+// moves 48 KB per stage through a 4-deep ring). Both CTAs' copies complete
+// on the leader's (rank 0's) "full" barrier, the leader's single MMA thread
+// issues M = 256 MMAs, and their commits reach both CTAs' "empty" and
+// accumulator barriers; both CTAs' epilogue warps release the accumulator on
+// the leader's barrier. Block-scaled kinds: each CTA also stages the scale
+// atoms of its 128 A rows and of all 256 B^T rows; the leader copies them
+// into the same TMEM columns of both CTAs (tcgen05.cp cta_group::2), and the
+// accumulator is single-buffered so the scale factors fit beside it. A
+// cluster barrier brackets set-up and tear-down so no CTA leaves while its
+// partner may still signal it.
 constexpr int P_BM = 256, P_BN = 256;
 constexpr uint32_t P_A_BYTES = 128 * BKB;  // this CTA's 128 rows of A
 constexpr uint32_t P_B_BYTES = 128 * BKB;  // this CTA's 128 rows of B^T
-struct SmemPair {
+
+template <int KIND>
+struct PairCfg {
+  using SF = SfCfg<KIND>;
+  static constexpr uint32_t kSfa = SF::A_SF;  // scale atoms of this CTA's 128 A rows
+  static constexpr uint32_t kSfb = SF::B_SF;  // scale atoms of the tile's 256 B^T rows
+  static constexpr uint32_t kStageBytes = P_A_BYTES + P_B_BYTES + kSfa + kSfb;
+  static constexpr int kNacc = KIND == kPerTensor ? 2 : 1;  // accumulator buffers
+  static constexpr int kStages = KIND == kPerTensor ? 7 : (KIND == kMxfp8 ? 6 : 5);
   static constexpr uint32_t kA = 0;
-  static constexpr uint32_t kB = kA + P_STAGES * P_A_BYTES;
-  static constexpr uint32_t kBar = kB + P_STAGES * P_B_BYTES;
-  static constexpr uint32_t kNumBars = 2 * P_STAGES + 5;  // full, empty, 2 x acc full/empty, drain
+  static constexpr uint32_t kB = kA + kStages * P_A_BYTES;
+  static constexpr uint32_t kSfA = kB + kStages * P_B_BYTES;
+  static constexpr uint32_t kSfB = kSfA + kStages * kSfa;
+  static constexpr uint32_t kBar = kSfB + kStages * kSfb;
+  static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNacc + 1;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
+  static_assert(kAlloc <= 227 * 1024, "pair ring exceeds shared memory");
+  static_assert(kNacc * 256 + (KIND == kPerTensor ? 0
+                                                  : kStages * (SF::SFA_COLS + SF::SFB_COLS)) <=
+                    TMEM_COLS,
+                "TMEM overflow");
 };
 
-template <int AFMT, int BFMT, int OUT>
+template <int KIND, int AFMT, int BFMT, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmap_a,
-                const __grid_constant__ CUtensorMap tmap_b, const Params p) {
-  using L = SmemPair;
+                const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_sfa,
+                const __grid_constant__ CUtensorMap tmap_sfb, const Params p) {
+  using C = PairCfg<KIND>;
+  using SF = SfCfg<KIND>;
+  constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* empty = full + P_STAGES;
-  uint64_t* tmem_full = empty + P_STAGES;  // two accumulator buffers of 256 columns
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* drain = tmem_empty + 2;
-  uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
-  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  uint64_t* empty = full + S;
+  uint64_t* tmem_full = empty + S;
+  uint64_t* tmem_empty = tmem_full + C::kNacc;
+  uint64_t* drain = tmem_empty + C::kNacc;
+  uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + C::kMisc);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMisc + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -399,11 +428,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_tiles = p.num_m * p.num_n;  // 256 x 256 tiles
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kNacc; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 2 * kEpiWarps);
     }
@@ -414,6 +443,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    if constexpr (KIND != kPerTensor) {
+      prefetch_tmap(&tmap_sfa);
+      prefetch_tmap(&tmap_sfb);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_base_sh, TMEM_COLS);
@@ -437,21 +470,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
+        // scale atoms (2-D copies of 512-byte rows; rows past the operand's
+        // end read as zeros): this CTA's 128 A rows and the tile's 256 B^T rows
+        const int a_atom = 2 * mb + (int)rank;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
             ok = false;
             break;
           }
           // the leader expects both CTAs' bytes on its own barrier
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
           const uint32_t fb = full_leader + 8u * stage;
-          tma_load_2d_pair(smem + L::kA + stage * P_A_BYTES, &tmap_a, kb * BKB,
+          tma_load_2d_pair(smem + C::kA + stage * P_A_BYTES, &tmap_a, kb * BKB,
                            mb * P_BM + 128 * (int)rank, fb);
-          tma_load_2d_pair(smem + L::kB + stage * P_B_BYTES, &tmap_b, kb * BKB,
+          tma_load_2d_pair(smem + C::kB + stage * P_B_BYTES, &tmap_b, kb * BKB,
                            nb * P_BN + 128 * (int)rank, fb);
+          if constexpr (KIND != kPerTensor) {
+            const int kcol = kb * (int)SF::kAtomsK;
+            tma_load_2d_pair(smem + C::kSfA + stage * C::kSfa, &tmap_sfa, 0,
+                             a_atom * (int)p.sf_col_tiles + kcol, fb);
+            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb, &tmap_sfb, 0,
+                             (2 * nb) * (int)p.sf_col_tiles + kcol, fb);
+            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb + C::kSfb / 2, &tmap_sfb, 0,
+                             (2 * nb + 1) * (int)p.sf_col_tiles + kcol, fb);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == P_STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
@@ -460,7 +505,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!ok && rank == 0) {
         // the leader's barriers count both CTAs' copies: wait (bounded) for
         // those in flight before the pair leaves
-        for (int s = 0; s < P_STAGES; ++s)
+        for (int s = 0; s < S; ++s)
           if (issued & (1u << s)) {
             const uint64_t t0 = globaltimer();
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
@@ -475,7 +520,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0, abuf = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      const uint32_t idesc = idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN);
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         // accumulator buffer abuf: free once both CTAs' epilogues read it
         if (!mbar_wait(&tmem_empty[abuf], acc_phase ^ 1u, abort_flag, p.status, 1u)) {
@@ -490,22 +534,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kA + stage * P_A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + L::kB + stage * P_B_BYTES);
+          const uint32_t a_addr = smem_u32(smem + C::kA + stage * P_A_BYTES);
+          const uint32_t b_addr = smem_u32(smem + C::kB + stage * P_B_BYTES);
+          uint32_t sfa_col = 0, sfb_col = 0;
+          if constexpr (KIND != kPerTensor) {
+            sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+            sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
+            const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
+            const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
 #pragma unroll
-          for (uint32_t k = 0; k < 4; ++k)
-            mma_f8f6f4_pair(dacc, desc_kmajor_sw128(a_addr + 32 * k),
-                            desc_kmajor_sw128(b_addr + 32 * k), idesc,
-                            (kb > 0 || k > 0) ? 1u : 0u);
+            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+              tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+              tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+              tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+            }
+          }
+#pragma unroll
+          for (uint32_t k = 0; k < 4; ++k) {
+            const uint64_t ad = desc_kmajor_sw128(a_addr + 32 * k);
+            const uint64_t bd = desc_kmajor_sw128(b_addr + 32 * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (KIND == kPerTensor) {
+              mma_f8f6f4_pair(dacc, ad, bd, idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN), acc);
+            } else if constexpr (KIND == kMxfp8) {
+              mma_mxf8f6f4_pair(dacc, ad, bd, idesc_block_scaled(AFMT, BFMT, P_BM, P_BN, 1u, k, k),
+                                sfa_col | (k << 30), sfb_col | (k << 30), acc);
+            } else {
+              mma_mxf4nvf4_4x_pair(dacc, ad, bd,
+                                   idesc_block_scaled(1u, 1u, P_BM, P_BN, 0u, 0u, 0u),
+                                   sfa_col + 4 * k, sfb_col + 8 * k, acc);
+            }
+          }
           tc_commit_pair(&empty[stage], 0x3);
-          if (++stage == P_STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
         tc_commit_pair(&tmem_full[abuf], 0x3);
-        if (++abuf == 2) {
+        if (++abuf == C::kNacc) {
           abuf = 0;
           acc_phase ^= 1u;
         }
@@ -521,7 +589,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int half = ew / 4;    // which 128 accumulator columns
-    const float scale = __fmul_rn(*p.a_scale, *p.b_scale);
+    float scale = 1.f;
+    if constexpr (KIND == kPerTensor) scale = __fmul_rn(*p.a_scale, *p.b_scale);
     uint32_t acc_phase = 0;
     int abuf = 0;
     for (int tile = cluster; tile < num_tiles; tile += nclusters) {
@@ -537,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tmem_empty_leader + 8u * abuf);
-      if (++abuf == 2) {
+      if (++abuf == C::kNacc) {
         abuf = 0;
         acc_phase ^= 1u;
       }
@@ -548,7 +617,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__uint_as_float(r[c][i]), scale);
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __uint_as_float(r[c][i]);
+            if constexpr (KIND == kPerTensor) v[i] = __fmul_rn(v[i], scale);
+          }
           store_row_chunk<OUT>(p.d, p.ldd, row, col0 + 32 * c, p.N, v, 32);
         }
       }
@@ -810,10 +882,11 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
   return check_launch();
 }
 
-template <int AFMT, int BFMT, int OUT>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
-  auto kern = k_gemm_pair<AFMT, BFMT, OUT>;
-  const int smem = (int)SmemPair::kAlloc;
+template <int KIND, int AFMT, int BFMT, int OUT>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                const CUtensorMap& tsb, const Params& p, cudaStream_t st) {
+  auto kern = k_gemm_pair<KIND, AFMT, BFMT, OUT>;
+  const int smem = (int)PairCfg<KIND>::kAlloc;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -826,16 +899,37 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, c
   const int tiles = p.num_m * p.num_n;
   const int pairs = sm_count() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, tsa, tsb, p);
   return check_launch();
 }
 
-template <int AFMT, int BFMT>
-int launch_pair_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+template <int KIND, int AFMT, int BFMT>
+int launch_pair_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb,
+                    const CUtensorMap& tsa, const CUtensorMap& tsb, const Params& p,
                     cudaStream_t st) {
-  if (out_dtype == BRC_DTYPE_F32) return launch_pair<AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, p, st);
-  if (out_dtype == BRC_DTYPE_BF16) return launch_pair<AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, p, st);
-  return launch_pair<AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, p, st);
+  if (out_dtype == BRC_DTYPE_F32)
+    return launch_pair<KIND, AFMT, BFMT, BRC_DTYPE_F32>(ta, tb, tsa, tsb, p, st);
+  if (out_dtype == BRC_DTYPE_BF16)
+    return launch_pair<KIND, AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, tsa, tsb, p, st);
+  return launch_pair<KIND, AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, tsa, tsb, p, st);
+}
+
+// Scale atoms (512 bytes each, row group-major) as a 2-D tensor of rows of
+// 128 uint32 values; a box is `atoms_k` consecutive atoms.
+int make_sf_tmap(CUtensorMap* m, const uint8_t* sf, int row_groups, uint32_t col_tiles,
+                 uint32_t atoms_k) {
+  return encode_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, sf, 128,
+                        (uint64_t)row_groups * col_tiles, 512, 128, atoms_k);
+}
+
+// CTA pairs (256 x 256 tiles) when they fill the GPU, single CTAs otherwise.
+bool use_pairs(int M, int N) {
+  return ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN) >= sm_count() / 2;
+}
+void to_pair_params(Params& p) {
+  p.num_m = (p.M + P_BM - 1) / P_BM;
+  p.num_n = (p.N + P_BN - 1) / P_BN;
+  p.group_m = kGroupM / 2;  // the same 2048 rows of A per tile group
 }
 
 template <int KIND, int AFMT, int BFMT>
@@ -886,13 +980,6 @@ int check_common(const void* a, const void* b, void* d, int M, int N, int K, int
   return BRC_OK;
 }
 
-// Tiles are visited in groups of kGroupM row blocks, row block fastest: the
-// CTAs in flight share kGroupM A panels (BM x K) and about 148 / kGroupM B
-// panels (BN x K); A is read from DRAM about once and B about num_m / kGroupM
-// times (C2, 16384 x 8192 x 8192: 664 MB read per launch). Measured on B200:
-// 32 raised the reads to 1.5 GB and slowed the MXFP8 GEMM of 8192 x 28672 x
-// 8192 from 1.63 to 2.18 ms; 4 and 8 were 3-15% slower than 16.
-constexpr int kGroupM = 16;
 
 Params base_params(int M, int N, int K, int k_per_stage, void* d) {
   Params p{};
@@ -968,23 +1055,21 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
   if (K == 0) return BRC_ERR_UNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
   CUtensorMap ta, tb;
-  // CTA pairs (256 x 256 tiles) when they fill the GPU, single CTAs else
-  const int pair_tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
-  if (pair_tiles >= sm_count() / 2) {
+  if (use_pairs(M, N)) {
     if ((rc = make_tmap(&ta, a, M, K, 128))) return rc;
     if ((rc = make_tmap(&tb, b, N, K, 128))) return rc;
     Params p = base_params(M, N, K, BKB, d);
-    p.num_m = (M + P_BM - 1) / P_BM;
-    p.num_n = (N + P_BN - 1) / P_BN;
-    p.group_m = kGroupM / 2;  // the same 2048 rows of A per tile group
+    to_pair_params(p);
     p.a_scale = a_scale;
     p.b_scale = b_scale;
     p.status = status_word();
     if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
-      return launch_pair_out<0, 0>(d_dtype, ta, tb, p, st);
-    if (a_fmt == BRC_FP8_E4M3) return launch_pair_out<0, 1>(d_dtype, ta, tb, p, st);
-    if (b_fmt == BRC_FP8_E4M3) return launch_pair_out<1, 0>(d_dtype, ta, tb, p, st);
-    return launch_pair_out<1, 1>(d_dtype, ta, tb, p, st);
+      return launch_pair_out<kPerTensor, 0, 0>(d_dtype, ta, tb, ta, tb, p, st);
+    if (a_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<kPerTensor, 0, 1>(d_dtype, ta, tb, ta, tb, p, st);
+    if (b_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<kPerTensor, 1, 0>(d_dtype, ta, tb, ta, tb, p, st);
+    return launch_pair_out<kPerTensor, 1, 1>(d_dtype, ta, tb, ta, tb, p, st);
   }
   if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
   if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
@@ -1013,15 +1098,35 @@ int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int 
   if ((int64_t)M * N == 0) return BRC_OK;
   if (K == 0) return BRC_ERR_UNSUPPORTED;
   CUtensorMap ta, tb;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t sf_col_tiles = (uint32_t)((K / 32 + 3) / 4);
+  if (use_pairs(M, N)) {
+    CUtensorMap tsa, tsb;
+    if ((rc = make_tmap(&ta, a, M, K, 128))) return rc;
+    if ((rc = make_tmap(&tb, b, N, K, 128))) return rc;
+    if ((rc = make_sf_tmap(&tsa, a_sf_mma, (M + 127) / 128, sf_col_tiles, 1))) return rc;
+    if ((rc = make_sf_tmap(&tsb, b_sf_mma, (N + 127) / 128, sf_col_tiles, 1))) return rc;
+    Params p = base_params(M, N, K, BKB, d);
+    to_pair_params(p);
+    p.sf_col_tiles = sf_col_tiles;
+    p.sfb_row_atoms = (N + 127) / 128;
+    p.status = status_word();
+    if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<kMxfp8, 0, 0>(d_dtype, ta, tb, tsa, tsb, p, st);
+    if (a_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<kMxfp8, 0, 1>(d_dtype, ta, tb, tsa, tsb, p, st);
+    if (b_fmt == BRC_FP8_E4M3)
+      return launch_pair_out<kMxfp8, 1, 0>(d_dtype, ta, tb, tsa, tsb, p, st);
+    return launch_pair_out<kMxfp8, 1, 1>(d_dtype, ta, tb, tsa, tsb, p, st);
+  }
   if ((rc = make_tmap(&ta, a, M, K, BM))) return rc;
   if ((rc = make_tmap(&tb, b, N, K, BN))) return rc;
   Params p = base_params(M, N, K, BKB, d);
   p.sfa = a_sf_mma;
   p.sfb = b_sf_mma;
-  p.sf_col_tiles = (uint32_t)((K / 32 + 3) / 4);
+  p.sf_col_tiles = sf_col_tiles;
   p.sfb_row_atoms = (N + 127) / 128;
   p.status = status_word();
-  cudaStream_t st = (cudaStream_t)stream;
   if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
     return launch_out<kMxfp8, 0, 0>(d_dtype, ta, tb, p, st);
   if (a_fmt == BRC_FP8_E4M3) return launch_out<kMxfp8, 0, 1>(d_dtype, ta, tb, p, st);
@@ -1040,12 +1145,31 @@ int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int 
   if ((int64_t)M * N == 0) return BRC_OK;
   if (K == 0) return BRC_ERR_UNSUPPORTED;
   CUtensorMap ta, tb;
+  const uint32_t sf_col_tiles = (uint32_t)((K / 16 + 3) / 4);
+  // The pair form stays off for NVFP4: its 256 x 256 tiles last ~2 us, and
+  // with the scale factors beside it the accumulator cannot be double
+  // buffered, so the per-tile hand-off to the epilogue costs more than the
+  // pair saves (measured: 0.599 vs 0.566 ms on 4096 x 28672 x 8192).
+  constexpr bool kNvfp4Pairs = false;
+  if (kNvfp4Pairs && use_pairs(M, N)) {
+    CUtensorMap tsa, tsb;
+    if ((rc = make_tmap(&ta, a_packed, M, K / 2, 128))) return rc;
+    if ((rc = make_tmap(&tb, b_packed, N, K / 2, 128))) return rc;
+    if ((rc = make_sf_tmap(&tsa, a_sf_mma, (M + 127) / 128, sf_col_tiles, 4))) return rc;
+    if ((rc = make_sf_tmap(&tsb, b_sf_mma, (N + 127) / 128, sf_col_tiles, 4))) return rc;
+    Params p = base_params(M, N, K, 2 * BKB, d);
+    to_pair_params(p);
+    p.sf_col_tiles = sf_col_tiles;
+    p.sfb_row_atoms = (N + 127) / 128;
+    p.status = status_word();
+    return launch_pair_out<kNvfp4, 0, 0>(d_dtype, ta, tb, tsa, tsb, p, (cudaStream_t)stream);
+  }
   if ((rc = make_tmap(&ta, a_packed, M, K / 2, BM))) return rc;
   if ((rc = make_tmap(&tb, b_packed, N, K / 2, BN))) return rc;
   Params p = base_params(M, N, K, 2 * BKB, d);
   p.sfa = a_sf_mma;
   p.sfb = b_sf_mma;
-  p.sf_col_tiles = (uint32_t)((K / 16 + 3) / 4);
+  p.sf_col_tiles = sf_col_tiles;
   p.sfb_row_atoms = (N + 127) / 128;
   p.status = status_word();
   return launch_out<kNvfp4, 0, 0>(d_dtype, ta, tb, p, (cudaStream_t)stream);

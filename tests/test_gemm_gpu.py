@@ -104,14 +104,17 @@ def test_linear_vs_oracle(kind, M, N, K):
     _check(out.cpu().numpy(), ref, tight=1e-5)
 
 
-@pytest.mark.parametrize("kind", ["current", "delayed_e5m2"])
+@pytest.mark.parametrize("kind", ["current", "delayed_e5m2", "mxfp8", "mxfp8_e5m2", "nvfp4"])
 @pytest.mark.parametrize("M,N,K", [(2048, 2560, 512), (2000, 2576, 384), (4096, 4864, 256)])
-def test_per_tensor_cta_pair_path(kind, M, N, K):
-    """Shapes large enough for the CTA-pair GEMM (256 x 256 tiles, at least
-    one per SM pair): ragged M and N, several tiles per pair."""
+def test_cta_pair_path(kind, M, N, K):
+    """Shapes large enough for the CTA-pair GEMMs (256 x 256 tiles, at least
+    one per SM pair): ragged M and N (scale atoms past the operand's end),
+    several tiles per pair."""
     from oracle import cast as ocast
+    if kind == "nvfp4" and K % 256:
+        pytest.skip("NVFP4 GEMM needs K % 256 == 0")
     r = _recipe(kind)
-    A, W = _operands(M, N, K, seed=M + N + K + 7)
+    A, W = _operands(M, N, K, seed=M + N + K + 7, heavy=(kind == "nvfp4"))
     sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
     out = bb().linear(sa, sw, out_dtype=torch.float32)
     torch.cuda.synchronize()
