@@ -554,6 +554,13 @@ def per_recipe(peaks, src):
         gbs = bytes_ / (ms * 1e-3) / 1e9
         res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm}
 
+    def ste_entry(name, x, r, bytes_):
+        # fused cast_ste forward vs the unfused cast -> dequantize -> x + (y - x)
+        ms = _time_ms(lambda: bb.cast_ste(x, r))
+        ms_u = _time_ms(lambda: x + (bb.dequantize(bb.cast(x, r)) - x))
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm, "unfused_ms": ms_u}
+
     def gemm_entry(name, a, w, m, n, k, peak):
         ms = _time_ms(lambda: bb.linear(a, w, out_dtype=torch.bfloat16))
         tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
@@ -576,6 +583,7 @@ def per_recipe(peaks, src):
     # C2 per-tensor: A bf16 (16384, 8192): two reads + one write
     A = torch.randn(16384, 8192, generator=g, device=dev).to(torch.bfloat16)
     cast_entry("c2_cast_A_pertensor_bf16", A, bb.Float8CurrentScaling(), A.numel() * 5)
+    ste_entry("c2_cast_ste_A_pertensor_bf16", A, bb.Float8CurrentScaling(), A.numel() * 8)
     del A
     # C3 MXFP8: A bf16 (8192, 8192), W^T bf16 (28672, 8192); GEMM 8192 x 28672 x 8192
     r = bb.MXFP8BlockScaling()
@@ -583,6 +591,7 @@ def per_recipe(peaks, src):
     Wt = (torch.randn(28672, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     cast_entry("c3_cast_A_mxfp8_bf16", A, r, A.numel() * 3 + A.numel() // 32 * 2)
     cast_entry("c3_cast_Wt_mxfp8_bf16", Wt, r, Wt.numel() * 3 + Wt.numel() // 32 * 2)
+    ste_entry("c3_cast_ste_A_mxfp8_bf16", A, r, A.numel() * 6)
     gemm_entry("c3_gemm_mxfp8", bb.cast(A, r), bb.cast(Wt, r), 8192, 28672, 8192, fp8)
     del A, Wt
     # C4 NVFP4: A bf16 (4096, 8192), W^T bf16 (28672, 8192) Student-t(4) * 0.02

@@ -18,6 +18,9 @@ _i = ctypes.c_int
 _i64 = ctypes.c_int64
 
 # name -> argument types (every function returns int status unless noted)
+# brc_cast_ste_block kinds
+STE_BLOCK_FP8, STE_MXFP8, STE_NVFP4, STE_INT4 = 0, 1, 2, 3
+
 PROTOTYPES = {
     "brc_status_string": ([_i], ctypes.c_char_p),
     "brc_last_cuda_error": ([], _i),
@@ -32,6 +35,8 @@ PROTOTYPES = {
     "brc_cast_mxfp8": ([_p, _i, _i64, _i64, _i, _p, _p, _p, _p], _i),
     "brc_cast_nvfp4": ([_p, _i, _i64, _i64, _p, _p, _p, _p, _p], _i),
     "brc_cast_int4": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
+    "brc_cast_ste_pertensor_fp8": ([_p, _i, _i64, _i, _p, _p, _p], _i),
+    "brc_cast_ste_block": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _i, _i, _p, _p], _i),
     "brc_dequant_pertensor_fp8": ([_p, _i64, _i, _p, _p, _i, _p], _i),
     "brc_dequant_block_fp8": ([_p, _i64, _i64, _i, _i, _i, _p, _p, _i, _p], _i),
     "brc_dequant_mxfp8": ([_p, _i64, _i64, _i, _p, _p, _i, _p], _i),

@@ -120,6 +120,9 @@ struct BlockCastArgs {
   uint8_t* packed_tiles;
   float* scale_tiles;
   float* zp_tiles;
+  // cast_ste: float32 x + (dequantize(cast(x)) - x), one per element; no
+  // codes or scales are written
+  float* ste_out;
 };
 
 template <int E>
@@ -127,10 +130,44 @@ struct LaneVals {
   float f[E];
 };
 
-// Encode one lane's E values given the block's scale; writes codes/packed.
-template <int MODE, int FMT, int E>
+// cast_ste output for one lane: each code's dequantized value y (decode x
+// the stored scale; asymmetric INT4 (q - zp) x scale, as cast.py:574-586) and
+// x + (y - x) in float32, as the reference's x + (y - x).detach() evaluates it.
+template <int MODE, int FMT, int NW>
+__device__ __forceinline__ void ste_store(const BlockCastArgs& a, int64_t e0, const float* f,
+                                          const uint32_t* w, float dqs, float dqz) {
+  float o[4 * NW];
+#pragma unroll
+  for (int j = 0; j < NW; ++j) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t code = (w[j] >> (8 * i)) & 0xFFu;
+      float d;
+      if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
+        d = dec_fp8<FMT>(code);
+      } else if constexpr (MODE == kNvfp4) {
+        d = dec_e2m1(code);
+      } else {
+        const uint32_t lo = code & 0xFu;
+        d = (MODE == kInt4Sym && a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+        if constexpr (MODE == kInt4Asym) d = __fsub_rn(d, dqz);
+      }
+      const float x = f[4 * j + i];
+      o[4 * j + i] = __fadd_rn(x, __fsub_rn(__fmul_rn(d, dqs), x));
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4 * NW; k += 4)
+    stg16(a.ste_out + e0 + k, make_uint4(__float_as_uint(o[k]), __float_as_uint(o[k + 1]),
+                                         __float_as_uint(o[k + 2]), __float_as_uint(o[k + 3])));
+}
+
+// Encode one lane's E values given the block's scale; writes codes/packed
+// (or, STE, the cast_ste values with the stored scale dqs and zero point dqz).
+template <int MODE, int FMT, int E, bool STE = false>
 __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, const float* f,
-                                            float s, float zp, bool fast, int64_t tile_off) {
+                                            float s, float zp, bool fast, int64_t tile_off,
+                                            float dqs = 0.f, float dqz = 0.f) {
   constexpr int NW = E / 4;
   uint32_t w[NW];
   if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
@@ -157,6 +194,10 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
         w[j] = c;
       }
     }
+    if constexpr (STE) {
+      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      return;
+    }
     store_words<NW>(a.codes + e0, w);
   } else if constexpr (MODE == kNvfp4) {
     if (fast) {
@@ -173,6 +214,10 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
         for (int i = 0; i < 4; ++i) c |= enc1_e2m1(div_ieee(f[4 * j + i], s)) << (8 * i);
         w[j] = c;
       }
+    }
+    if constexpr (STE) {
+      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      return;
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
     if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
@@ -214,6 +259,10 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
         w[j] = c;
       }
     }
+    if constexpr (STE) {
+      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      return;
+    }
     if (a.codes) store_words<NW>(a.codes + e0, w);
     if (a.packed) store_packed<NW>(a.packed + e0 / 2, w);
     if (a.packed_tiles) {
@@ -228,7 +277,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
   }
 }
 
-template <int DT, int MODE, int FMT, int B, int LPB>
+template <int DT, int MODE, int FMT, int B, int LPB, bool STE = false>
 __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
   constexpr int V = In<DT>::kVec;
   constexpr int E = B / LPB;
@@ -291,18 +340,21 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
     for (int i = 0; i < NV; ++i) unpack<DT>(v[i], f + i * V);
 
     float s, zp = 0.f;
+    float dqs = 0.f, dqz = 0.f;  // stored scale / zero point (what dequantize uses)
     bool fast;
     if constexpr (MODE == kBlockFp8) {
       constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
       s = div_const(fmax_nan(st0, 1e-10f), kMax, FMT == BRC_FP8_E4M3 ? kRcp448 : kRcp57344);
-      if (part == 0) static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      if (!STE && part == 0) static_cast<float*>(a.scales)[blk] = canon_nan(s);
+      dqs = s;
       fast = isfinite(s);
     } else if constexpr (MODE == kMxfp8) {
       constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
       const float am = fmax_nan(st0, 1e-10f);
       const uint32_t e =
           e8m0_code(div_const(am, kMax, FMT == BRC_FP8_E4M3 ? kRcp448 : kRcp57344), g_e8m0_thr);
-      if (part == 0) {
+      dqs = e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127);
+      if (!STE && part == 0) {
         static_cast<uint8_t*>(a.scales)[blk] = (uint8_t)e;
         if (a.scales_mma) {
           const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
@@ -318,8 +370,9 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       const float am = fmax_nan(st0, 1e-10f);
       const uint32_t sc = enc1_e4m3(div_const(am, 6.f, kRcp6));
       float actual = dec_e4m3(sc);
+      dqs = actual;
       if (!(actual > 0.f)) actual = 0x1p-9f;  // np.where(actual > 0, actual, 2^-9)
-      if (part == 0) {
+      if (!STE && part == 0) {
         static_cast<uint8_t*>(a.scales)[blk] = (uint8_t)sc;
         if (a.scales_mma) {
           const uint32_t row = fdiv((uint32_t)blk, a.blocks_per_row);
@@ -332,7 +385,8 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
     } else if constexpr (MODE == kInt4Sym) {
       s = a.is_signed ? div_const(fmax_nan(st0, 1e-10f), 7.f, kRcp7)
                       : div_const(fmax_nan(st0, 1e-10f), 15.f, kRcp15);
-      if (part == 0) {
+      dqs = a.scale_f16 ? __half2float(__float2half_rn(s)) : s;
+      if (!STE && part == 0) {
         if (a.scale_f16) static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
         else static_cast<float*>(a.scales)[blk] = canon_nan(s);
       }
@@ -343,7 +397,9 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       const float zf = rintf(__fdiv_rn(-st0, s));
       // np.clip keeps the operand (including -0.0 and NaN) when it is in range
       zp = zf < 0.f ? 0.f : (zf > 15.f ? 15.f : zf);
-      if (part == 0) {
+      dqs = a.scale_f16 ? __half2float(__float2half_rn(s)) : s;
+      dqz = a.scale_f16 ? __half2float(__float2half_rn(zp)) : zp;
+      if (!STE && part == 0) {
         if (a.scale_f16) {
           static_cast<__half*>(a.scales)[blk] = to_half_canon(s);
           static_cast<__half*>(a.zp)[blk] = to_half_canon(zp);
@@ -355,7 +411,7 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       fast = isfinite(s) && isfinite(zp);
     }
     int64_t tile_off = 0;
-    if constexpr (MODE == kInt4Sym || MODE == kInt4Asym) {
+    if constexpr (!STE && (MODE == kInt4Sym || MODE == kInt4Asym)) {
       if (a.packed_tiles) {
         // tile (row / 16, group) of 16 rows x 64 bytes; per tile 16 fp32
         // scales (the stored value) and, asymmetric, 16 fp32 values 128 + the
@@ -376,7 +432,7 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
         }
       }
     }
-    encode_lane<MODE, FMT, E>(a, e0, f, s, zp, fast, tile_off);
+    encode_lane<MODE, FMT, E, STE>(a, e0, f, s, zp, fast, tile_off, dqs, dqz);
   }
 }
 
@@ -489,15 +545,21 @@ __device__ __forceinline__ float pertensor_scale(uint32_t bits, float fmt_max, f
   return __fdiv_rn(amax, fmt_max);
 }
 
-template <int DT, int FMT>
+// cast_ste value of one element: x + (dequantize(code) - x) in float32.
+template <int FMT>
+__device__ __forceinline__ float ste1(float x, uint32_t code, float scale) {
+  return __fadd_rn(x, __fsub_rn(__fmul_rn(dec_fp8<FMT>(code), scale), x));
+}
+
+template <int DT, int FMT, bool STE = false>
 __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict__ x, int64_t n,
                                                          const uint32_t* amax_bits,
                                                          float floor_scale, uint8_t* codes,
-                                                         float* scale_out) {
+                                                         float* scale_out, float* ste_out) {
   constexpr int V = In<DT>::kVec;
   constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
   const float s = pertensor_scale(*amax_bits, kMax, floor_scale);
-  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = canon_nan(s);
+  if (!STE && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = canon_nan(s);
   const bool fast = isfinite(s);
   const float r = __frcp_rn(s);
   const int64_t nvec = n / V;
@@ -519,8 +581,20 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
       for (int j = 0; j < V / 4; ++j)
         w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
                               div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
-      if constexpr (V == 8) stg8_last_use(codes + vi * V, w0[0], w0[1], pol);
-      else *reinterpret_cast<uint32_t*>(codes + vi * V) = w0[0];
+      if constexpr (STE) {
+#pragma unroll
+        for (int j = 0; j < V / 4; ++j) {
+          float o[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o[q] = ste1<FMT>(f0[4 * j + q], (w0[j] >> (8 * q)) & 0xFFu, s);
+          stg16(ste_out + vi * V + 4 * j, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]),
+                                                      __float_as_uint(o[2]), __float_as_uint(o[3])));
+        }
+      } else if constexpr (V == 8) {
+        stg8_last_use(codes + vi * V, w0[0], w0[1], pol);
+      } else {
+        *reinterpret_cast<uint32_t*>(codes + vi * V) = w0[0];
+      }
     };
     // four 16-byte vectors in flight per thread per iteration
     for (; i + 3 * stride < nvec; i += 4 * stride) {
@@ -537,11 +611,19 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
       float f0[V];
       unpack<DT>(ldg16(base + 16 * i), f0);
 #pragma unroll
-      for (int j = 0; j < V; ++j) codes[i * V + j] = (uint8_t)enc1_fp8<FMT>(div_ieee(f0[j], s));
+      for (int j = 0; j < V; ++j) {
+        const uint32_t c = enc1_fp8<FMT>(div_ieee(f0[j], s));
+        if constexpr (STE) ste_out[i * V + j] = ste1<FMT>(f0[j], c, s);
+        else codes[i * V + j] = (uint8_t)c;
+      }
     }
   }
-  for (int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
-    codes[t] = (uint8_t)enc1_fp8<FMT>(div_ieee(load1<DT>(x, t), s));
+  for (int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride) {
+    const float xv = load1<DT>(x, t);
+    const uint32_t c = enc1_fp8<FMT>(div_ieee(xv, s));
+    if constexpr (STE) ste_out[t] = ste1<FMT>(xv, c, s);
+    else codes[t] = (uint8_t)c;
+  }
 }
 
 // --------------------------------------------------------------- 2-D tiles
@@ -969,7 +1051,7 @@ int dispatch_dt_fmt(int dt, int fmt, Args... args) {
 // block, choosing LPB so each lane owns 64 bytes (32 halves / 16 floats), or
 // the whole block when it is smaller. The per-block work (statistic, scale,
 // scale stores) then runs on as few lanes as possible.
-template <int DT, int MODE, int FMT, int B>
+template <int DT, int MODE, int FMT, int B, bool STE = false>
 int launch_block_b(const BlockCastArgs& a, cudaStream_t st) {
   constexpr int V = In<DT>::kVec;
   constexpr int E0 = (DT == BRC_DTYPE_F32) ? 16 : 32;  // 64 bytes per lane
@@ -978,21 +1060,21 @@ int launch_block_b(const BlockCastArgs& a, cudaStream_t st) {
   static_assert(E % V == 0 && LPB >= 1 && LPB <= 32, "bad lane split");
   const int64_t tiles = (a.n_blocks + (32 / LPB) - 1) / (32 / LPB);
   const int grid = grid_for(tiles, 8);
-  k_block_cast<DT, MODE, FMT, B, LPB><<<grid, 256, 0, st>>>(a);
+  k_block_cast<DT, MODE, FMT, B, LPB, STE><<<grid, 256, 0, st>>>(a);
   return check_launch();
 }
 
-template <int DT, int MODE, int FMT>
+template <int DT, int MODE, int FMT, bool STE = false>
 int launch_block(const BlockCastArgs& a, int B, cudaStream_t st) {
   switch (B) {
-    case 16: return launch_block_b<DT, MODE, FMT, 16>(a, st);
-    case 32: return launch_block_b<DT, MODE, FMT, 32>(a, st);
-    case 64: return launch_block_b<DT, MODE, FMT, 64>(a, st);
-    case 128: return launch_block_b<DT, MODE, FMT, 128>(a, st);
-    case 256: return launch_block_b<DT, MODE, FMT, 256>(a, st);
+    case 16: return launch_block_b<DT, MODE, FMT, 16, STE>(a, st);
+    case 32: return launch_block_b<DT, MODE, FMT, 32, STE>(a, st);
+    case 64: return launch_block_b<DT, MODE, FMT, 64, STE>(a, st);
+    case 128: return launch_block_b<DT, MODE, FMT, 128, STE>(a, st);
+    case 256: return launch_block_b<DT, MODE, FMT, 256, STE>(a, st);
     default: break;
   }
-  if (MODE == kBlockFp8 || MODE == kInt4Sym || MODE == kInt4Asym) {
+  if (!STE && (MODE == kBlockFp8 || MODE == kInt4Sym || MODE == kInt4Asym)) {
     if (a.packed && (B & 1)) return BRC_ERR_UNSUPPORTED;
     k_block_cast_generic<DT, MODE, FMT>
         <<<grid_for(a.n_blocks, 256), 256, 0, st>>>(a, B);
@@ -1001,11 +1083,11 @@ int launch_block(const BlockCastArgs& a, int B, cudaStream_t st) {
   return BRC_ERR_UNSUPPORTED;
 }
 
-template <int MODE, int FMT>
+template <int MODE, int FMT, bool STE = false>
 int launch_block_any_dt(int dt, const BlockCastArgs& a, int B, cudaStream_t st) {
-  if (dt == BRC_DTYPE_F32) return launch_block<BRC_DTYPE_F32, MODE, FMT>(a, B, st);
-  if (dt == BRC_DTYPE_BF16) return launch_block<BRC_DTYPE_BF16, MODE, FMT>(a, B, st);
-  return launch_block<BRC_DTYPE_F16, MODE, FMT>(a, B, st);
+  if (dt == BRC_DTYPE_F32) return launch_block<BRC_DTYPE_F32, MODE, FMT, STE>(a, B, st);
+  if (dt == BRC_DTYPE_BF16) return launch_block<BRC_DTYPE_BF16, MODE, FMT, STE>(a, B, st);
+  return launch_block<BRC_DTYPE_F16, MODE, FMT, STE>(a, B, st);
 }
 
 // Empty inputs are valid no-ops (their data pointers may be NULL).
@@ -1070,7 +1152,7 @@ struct PerTensorApply {
     const int V = In<DT>::kVec;
     const int grid = grid_for(n / V + 1, 256 * 4);
     k_pertensor_apply<DT, FMT><<<grid, 256, 0, st>>>(x, n, amax_bits, floor_scale, codes,
-                                                     scale_out);
+                                                     scale_out, nullptr);
     return check_launch();
   }
 };
@@ -1252,6 +1334,73 @@ int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int gr
   cudaStream_t st = (cudaStream_t)stream;
   return symmetric ? launch_block_any_dt<kInt4Sym, 0>(x_dtype, a, group, st)
                    : launch_block_any_dt<kInt4Asym, 0>(x_dtype, a, group, st);
+}
+
+// ---------------------------------------------------------------- cast_ste
+}  // extern "C"
+namespace {
+template <int DT, int FMT>
+struct PerTensorSte {
+  static int run(const void* x, int64_t n, const uint32_t* amax_bits, float* out,
+                 cudaStream_t st) {
+    const double fmax = FMT == BRC_FP8_E4M3 ? 448.0 : 57344.0;
+    const float floor_scale = (float)(1e-10 / fmax);
+    const int grid = grid_for(n / In<DT>::kVec + 1, 256 * 4);
+    k_pertensor_apply<DT, FMT, true>
+        <<<grid, 256, 0, st>>>(x, n, amax_bits, floor_scale, nullptr, nullptr, out);
+    return check_launch();
+  }
+};
+}  // namespace
+extern "C" {
+
+int brc_cast_ste_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt,
+                               uint32_t* amax_word, float* out, void* stream) {
+  if (!amax_word || ((!x || !out) && n > 0)) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype) || !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (n < 0) return BRC_ERR_SHAPE;
+  if (n == 0) return BRC_OK;
+  if (!aligned16(x) || !aligned16(out)) return BRC_ERR_ALIGN;
+  int rc = brc_amax_reset(amax_word, stream);
+  if (rc) return rc;
+  if ((rc = brc_amax_accumulate(x, x_dtype, n, amax_word, stream))) return rc;
+  return dispatch_dt_fmt<PerTensorSte>(x_dtype, fmt, x, n, amax_word, out, (cudaStream_t)stream);
+}
+
+int brc_cast_ste_block(const void* x, int x_dtype, int64_t rows, int64_t cols, int kind,
+                       int block, int fmt, int is_signed, int symmetric, int scale_dtype,
+                       float* out, void* stream) {
+  int rc = common_checks(x, x_dtype, rows, cols, block);
+  if (rc) return rc;
+  if (kind == BRC_STE_MXFP8 && block != 32) return BRC_ERR_UNSUPPORTED;
+  if (kind == BRC_STE_NVFP4 && block != 16) return BRC_ERR_UNSUPPORTED;
+  if ((kind == BRC_STE_BLOCK_FP8 || kind == BRC_STE_MXFP8) && !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (kind == BRC_STE_INT4 && !symmetric && is_signed) return BRC_ERR_UNSUPPORTED;
+  if (kind == BRC_STE_INT4 && scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32)
+    return BRC_ERR_DTYPE;
+  if (kind < BRC_STE_BLOCK_FP8 || kind > BRC_STE_INT4) return BRC_ERR_UNSUPPORTED;
+  if (empty_input(rows, cols, block)) return BRC_OK;
+  if (!out) return BRC_ERR_NULL;
+  if (!aligned16(out)) return BRC_ERR_ALIGN;
+  BlockCastArgs a = make_args(x, rows, cols, block);
+  a.ste_out = out;
+  a.is_signed = is_signed ? 1 : 0;
+  a.scale_f16 = scale_dtype == BRC_SCALE_F16;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool e4 = fmt == BRC_FP8_E4M3;
+  switch (kind) {
+    case BRC_STE_BLOCK_FP8:
+      return e4 ? launch_block_any_dt<kBlockFp8, BRC_FP8_E4M3, true>(x_dtype, a, block, st)
+                : launch_block_any_dt<kBlockFp8, BRC_FP8_E5M2, true>(x_dtype, a, block, st);
+    case BRC_STE_MXFP8:
+      return e4 ? launch_block_any_dt<kMxfp8, BRC_FP8_E4M3, true>(x_dtype, a, block, st)
+                : launch_block_any_dt<kMxfp8, BRC_FP8_E5M2, true>(x_dtype, a, block, st);
+    case BRC_STE_NVFP4:
+      return launch_block_any_dt<kNvfp4, 0, true>(x_dtype, a, block, st);
+    default:
+      return symmetric ? launch_block_any_dt<kInt4Sym, 0, true>(x_dtype, a, block, st)
+                       : launch_block_any_dt<kInt4Asym, 0, true>(x_dtype, a, block, st);
+  }
 }
 
 // ---------------------------------------------------------------- dequant

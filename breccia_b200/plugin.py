@@ -2,8 +2,9 @@
 
 breccia has no registry: its public functions are plain module attributes
 (``src/breccia/__init__.py:23`` re-exports ``cast, dequantize, requantize,
-matmul`` from ``breccia.kernels.reference``; ``breccia/autograd.py:47``
-imports ``cast`` and ``dequantize`` by name). ``install()`` rebinds each of
+matmul`` from ``breccia.kernels.reference`` and ``__init__.py:24``
+``cast_ste, cast_ste_clipped`` from ``breccia.autograd``;
+``breccia/autograd.py:47`` imports ``cast`` and ``dequantize`` by name). ``install()`` rebinds each of
 those names to a wrapper that sends CUDA torch inputs to breccia_b200 and
 calls breccia's original function for everything else (NumPy, CPU torch,
 JAX, MLX). ``uninstall()`` restores the originals.
@@ -15,11 +16,11 @@ import functools
 import importlib
 
 _SITES = [
-    ("breccia", ("cast", "dequantize", "requantize", "matmul")),
+    ("breccia", ("cast", "dequantize", "requantize", "matmul", "cast_ste", "cast_ste_clipped")),
     ("breccia.kernels.reference", ("cast", "dequantize", "requantize", "matmul")),
     ("breccia.kernels.reference.cast", ("cast", "dequantize", "requantize")),
     ("breccia.kernels.reference.matmul", ("dequantize",)),
-    ("breccia.autograd", ("cast", "dequantize")),
+    ("breccia.autograd", ("cast", "dequantize", "cast_ste", "cast_ste_clipped")),
 ]
 _saved: dict = {}
 
@@ -33,9 +34,9 @@ def _on_cuda(obj) -> bool:
 
 
 def _wrap(name, original):
-    from . import api
+    from . import api, autograd
 
-    ours = getattr(api, name)
+    ours = getattr(autograd if name.startswith("cast_ste") else api, name)
 
     @functools.wraps(original)
     def dispatch(*args, **kwargs):

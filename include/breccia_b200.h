@@ -160,6 +160,29 @@ int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int gr
                   uint8_t* packed, void* scales, void* zero_points, uint8_t* packed_tiles,
                   float* scale_tiles, float* zp_tiles, void* stream);
 
+/* ======================================================= cast_ste (fused)
+ * The forward value of breccia.autograd.cast_ste / cast_ste_clipped for one
+ * recipe in a single pass: out = x + (dequantize(cast(x, recipe)) - x) in
+ * float32, per element, with the codes and stored scales the cast would
+ * produce (src/breccia/autograd.py:84-87, 179-190; cast.py:364-586). No codes
+ * or scales are written. out: float32, same element count as x, 16-byte
+ * aligned.
+ * brc_cast_ste_pertensor_fp8: Float8CurrentScaling / DelayedScaling;
+ * amax_word: one uint32 of device scratch.
+ * brc_cast_ste_block: kind BRC_STE_BLOCK_FP8 (block = block_k), BRC_STE_MXFP8
+ * (block 32), BRC_STE_NVFP4 (block 16, fmt ignored), BRC_STE_INT4 (block =
+ * group; is_signed, symmetric, scale_dtype as brc_cast_int4). Block sizes
+ * 16/32/64/128/256; others return BRC_ERR_UNSUPPORTED. */
+#define BRC_STE_BLOCK_FP8 0
+#define BRC_STE_MXFP8 1
+#define BRC_STE_NVFP4 2
+#define BRC_STE_INT4 3
+int brc_cast_ste_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt,
+                               uint32_t* amax_word, float* out, void* stream);
+int brc_cast_ste_block(const void* x, int x_dtype, int64_t rows, int64_t cols, int kind,
+                       int block, int fmt, int is_signed, int symmetric, int scale_dtype,
+                       float* out, void* stream);
+
 /* ======================================================= dequantize
  * out = decode(code) * scale (asymmetric INT4: (code - zp) * scale), written as
  * float32 (the reference's dtype) or, as an extension, bf16/f16.

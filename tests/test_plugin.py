@@ -30,6 +30,9 @@ def fake_breccia(monkeypatch):
         m = types.ModuleType(modname)
         for fn in ("cast", "dequantize", "requantize", "matmul"):
             setattr(m, fn, mk(f"{modname}.{fn}"))
+        if modname in ("breccia", "breccia.autograd"):
+            for fn in ("cast_ste", "cast_ste_clipped"):
+                setattr(m, fn, mk(f"{modname}.{fn}"))
         mods[modname] = m
         monkeypatch.setitem(sys.modules, modname, m)
     yield mods, calls
@@ -48,6 +51,19 @@ def test_install_routes_cpu_inputs_to_breccia(fake_breccia):
     plugin.uninstall()
     assert not getattr(mods["breccia"].cast, "__breccia_b200__", False)
     assert mods["breccia"].cast(x, None) == "breccia.cast"
+
+
+def test_install_rebinds_cast_ste(fake_breccia):
+    mods, calls = fake_breccia
+    breccia_b200.install()
+    for modname in ("breccia", "breccia.autograd"):
+        for fn in ("cast_ste", "cast_ste_clipped"):
+            f = getattr(mods[modname], fn)
+            assert getattr(f, "__breccia_b200__", False)
+            # non-CUDA inputs keep breccia's own function
+            assert f(np.zeros((2, 32), np.float32), None) == f"{modname}.{fn}"
+    plugin.uninstall()
+    assert mods["breccia"].cast_ste(np.zeros(1), None) == "breccia.cast_ste"
 
 
 def test_cuda_check_without_gpu():
