@@ -796,12 +796,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + pbuf * kPartialCols + 128 * half;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + 32 * c, r);
-          tmem_ld_wait();
+        for (int c = 0; c < 8; ++c) {
+          uint32_t ra[16];
+          tmem_ld16(taddr + 16 * c, ra);
+          tmem_ld_wait16(ra);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[32 * c + i] = __fmaf_rn(__uint_as_float(r[i]), s, acc[32 * c + i]);
+          for (int i = 0; i < 16; ++i) acc[16 * c + i] = __fmaf_rn(__uint_as_float(ra[i]), s, acc[16 * c + i]);
         }
         tc_fence_before();
         __syncwarp();
