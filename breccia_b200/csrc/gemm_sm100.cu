@@ -51,6 +51,12 @@ constexpr int BKB = 128;  // K bytes per stage (one 128-byte swizzle row)
 constexpr int STAGES = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
+// Single-CTA block-scaled GEMMs add one warp that copies the scale atoms
+// into TMEM (tcgen05.cp), so the copies are issued beside the MMA thread
+// rather than between its MMAs.
+constexpr bool kSfCopier = true;
+template <int KIND>
+constexpr int kThreadsG = kThreads + ((kSfCopier && KIND != 0) ? 32 : 0);
 constexpr uint32_t A_BYTES = BM * BKB;  // 16 KB
 constexpr uint32_t B_BYTES = BN * BKB;  // 32 KB
 // Tiles are visited in groups of kGroupM row blocks, row block fastest: the
@@ -81,10 +87,11 @@ struct Smem {
   static constexpr uint32_t kSfA = kB + STAGES * B_BYTES;
   static constexpr uint32_t kSfB = kSfA + STAGES * SfCfg<KIND>::A_SF;
   static constexpr uint32_t kBar = kSfB + STAGES * SfCfg<KIND>::B_SF;
-  static constexpr uint32_t kNumBars = 2 * STAGES + 8;  // stage ring + accumulator/partial/drain
+  static constexpr uint32_t kNumBars = 4 * STAGES + 8;  // stage ring, scale-factor ring, accumulator/partial/drain
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
+  static_assert(kAlloc <= 227 * 1024, "stage ring exceeds shared memory");
 };
 
 struct Params {
@@ -149,7 +156,7 @@ __device__ __forceinline__ void store_row_chunk(void* d, int64_t ldd, int row, i
 }
 
 template <int KIND, int AFMT, int BFMT, int OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsG<KIND>, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
            const Params p) {
   using SF = SfCfg<KIND>;
@@ -162,7 +169,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_full = empty + STAGES;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* drain = tmem_empty + 1;
-  static_assert(2 * STAGES + 3 <= L::kNumBars, "barrier area too small");
+  uint64_t* sf_full = drain + 1;        // scale factors of a stage are in TMEM
+  uint64_t* sf_free = sf_full + STAGES;  // the MMAs reading a stage's TMEM slot are done
+  uint64_t* cdrain = sf_free + STAGES;
+  constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
+  static_assert(4 * STAGES + 4 <= L::kNumBars, "barrier area too small");
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
 
@@ -178,6 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(tmem_full, 1);
     mbar_init(tmem_empty, kEpiWarps);
     mbar_init(drain, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sf_full[s], 1);
+      mbar_init(&sf_free[s], 1);
+    }
+    mbar_init(cdrain, 1);
     *abort_flag = 0u;
     fence_mbar_init();
   }
@@ -267,7 +283,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(smem + L::kA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(smem + L::kB + stage * B_BYTES);
           uint32_t sfa_col = 0, sfb_col = 0;
-          if constexpr (KIND != kPerTensor) {
+          if constexpr (kCopier) {
+            sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+            sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
+            if (!mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
             const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
@@ -296,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc_commit(&empty[stage]);
+          if constexpr (kCopier) tc_commit(&sf_free[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -309,6 +334,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else if (kCopier && warp == 2 + kEpiWarps) {
+    // ------------------------------------------------------------ scale-factor copier
+    // Copies each stage's scale atoms from shared memory into that stage's
+    // TMEM slot once the stage has landed and the MMAs that read the slot
+    // last have completed; its commit tells the MMA thread the slot is ready.
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) ||
+              !mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+          const uint32_t sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
+          const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
+          const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
+#pragma unroll
+          for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+            tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+            tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+            tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+          }
+          tc_commit(&sf_full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // every copy this thread issued has completed before TMEM is freed
+      tc_commit(cdrain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
       }
     }
   } else {
@@ -878,7 +943,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
   }
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kThreadsG<KIND>, smem, st>>>(ta, tb, p);
   return check_launch();
 }
 
