@@ -455,7 +455,9 @@ struct PairCfg {
   static constexpr uint32_t kSfA = kB + kStages * P_B_BYTES;
   static constexpr uint32_t kSfB = kSfA + kStages * kSfa;
   static constexpr uint32_t kBar = kSfB + kStages * kSfb;
-  static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNacc + 1;
+  // stage ring, accumulator barriers, drain, scale-factor ring (sf_full,
+  // sf_free) and the copier's drain
+  static constexpr uint32_t kNumBars = 4 * kStages + 2 * kNacc + 2;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
@@ -467,7 +469,7 @@ struct PairCfg {
 };
 
 template <int KIND, int AFMT, int BFMT, int OUT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_sfa,
@@ -483,6 +485,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* tmem_full = empty + S;
   uint64_t* tmem_empty = tmem_full + C::kNacc;
   uint64_t* drain = tmem_empty + C::kNacc;
+  uint64_t* sf_full = drain + 1;    // (leader) a stage's scale factors are in both CTAs' TMEM
+  uint64_t* sf_free = sf_full + S;  // (leader) the MMAs reading a stage's TMEM slot are done
+  uint64_t* cdrain = sf_free + S;
+  constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMisc + 4);
 
@@ -502,6 +508,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_empty[b], 2 * kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&sf_full[s], 1);
+      mbar_init(&sf_free[s], 1);
+    }
+    mbar_init(cdrain, 1);
     *abort_flag = 0u;
     fence_mbar_init();
   }
@@ -602,7 +613,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(smem + C::kA + stage * P_A_BYTES);
           const uint32_t b_addr = smem_u32(smem + C::kB + stage * P_B_BYTES);
           uint32_t sfa_col = 0, sfb_col = 0;
-          if constexpr (KIND != kPerTensor) {
+          if constexpr (kCopier) {
+            sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+            sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
+            if (!mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
             const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
@@ -631,6 +650,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
           }
           tc_commit_pair(&empty[stage], 0x3);
+          if constexpr (kCopier) tc_commit_pair(&sf_free[stage], 0x1);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -647,6 +667,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_commit_pair(drain, 0x1);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else if (kCopier && warp == 2 + kEpiWarps) {
+    // ------------------------------------------------------------ scale-factor copier (leader)
+    // The leader's full barrier counts both CTAs' copies, so once it completes
+    // both CTAs' scale atoms of the stage are in shared memory; each
+    // tcgen05.cp cta_group::2 moves every CTA's atoms into its own TMEM.
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) ||
+              !mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
+          const uint32_t sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
+          const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
+          const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
+#pragma unroll
+          for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+            tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+            tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+            tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+          }
+          tc_commit_pair(&sf_full[stage], 0x1);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // every copy issued has completed before the pair frees TMEM
+      tc_commit_pair(cdrain, 0x1);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
       }
     }
   } else {
@@ -964,7 +1024,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int tiles = p.num_m * p.num_n;
   const int pairs = sm_count() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, tsa, tsb, p);
+  kern<<<grid, kThreadsG<KIND>, smem, st>>>(ta, tb, tsa, tsb, p);
   return check_launch();
 }
 
