@@ -1271,11 +1271,10 @@ int brc_gemm_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, int M, int 
   if (K == 0) return BRC_ERR_UNSUPPORTED;
   CUtensorMap ta, tb;
   const uint32_t sf_col_tiles = (uint32_t)((K / 16 + 3) / 4);
-  // The pair form stays off for NVFP4: its 256 x 256 tiles last ~2 us, and
-  // with the scale factors beside it the accumulator cannot be double
-  // buffered, so the per-tile hand-off to the epilogue costs more than the
-  // pair saves (measured: 0.599 vs 0.566 ms on 4096 x 28672 x 8192).
-  constexpr bool kNvfp4Pairs = false;
+  // NVFP4 on CTA pairs: with both kernels' scale-factor copies on copier
+  // warps the pair form is ahead (4096 x 28672 x 8192: 0.513 vs 0.527 ms);
+  // before the copiers the single-CTA form was (0.599 vs 0.617 ms).
+  constexpr bool kNvfp4Pairs = true;
   if (kNvfp4Pairs && use_pairs(M, N)) {
     CUtensorMap tsa, tsb;
     if ((rc = make_tmap(&ta, a_packed, M, K / 2, 128))) return rc;
