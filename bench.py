@@ -608,7 +608,24 @@ def per_recipe(peaks, src):
     b = n * 1 + n // 16 + n * 1 + n // 32 * 2
     res["c4_requant_Wt_nvfp4_to_mxfp8"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
                                            "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
-    del A, Wt, sw
+    # loading the C4 weight from breccia's packed on-disk order (bridges): unpack to
+    # codes + tensor-core packed order, and rebuild the scale atoms
+    from breccia_b200 import _lib as L
+    st_ = torch.cuda.current_stream().cuda_stream
+    pk = torch.empty(n // 2, dtype=torch.uint8, device=dev)
+    L.call("brc_pack_nibbles_hi", sw.data.data_ptr(), n, pk.data_ptr(), st_)
+    codes_ = torch.empty(n, dtype=torch.uint8, device=dev)
+    lo_ = torch.empty(n // 2, dtype=torch.uint8, device=dev)
+    atoms_ = torch.empty(bb.gemm_operands(sw)["sf_mma"].numel(), dtype=torch.uint8, device=dev)
+
+    def _load_nvfp4():
+        L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes_.data_ptr(), lo_.data_ptr(), st_)
+        L.call("brc_scale_atoms", sw.scale.data_ptr(), 28672, 8192 // 16, atoms_.data_ptr(), st_)
+    ms = _time_ms(_load_nvfp4)
+    b = n // 2 + n // 16 + n + n // 2 + atoms_.numel()
+    res["c4_load_Wt_nvfp4_from_packed"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
+                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
+    del A, Wt, sw, pk, codes_, lo_, atoms_
     # C5 INT4 asymmetric g128: W^T f32 (28672, 8192)
     Wt = torch.randn(28672, 8192, generator=g, device=dev) * 0.02
     r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
@@ -616,6 +633,18 @@ def per_recipe(peaks, src):
                Wt.numel() * 5.5 + Wt.numel() // 128 * 4)
     sw = bb.cast(Wt, r)
     del Wt
+    # rebuilding the skinny-GEMM tiles of a stored (loaded) C5 weight
+    tl = bb.gemm_operands(sw)
+    n = sw.data.numel()
+
+    def _tiles():
+        L.call("brc_int4_tiles", sw.data.data_ptr(), 28672, 8192, sw.scale.data_ptr(),
+               sw.zero_point.data_ptr(), L.SCALE_F16, tl["int4_tiles"].data_ptr(),
+               tl["int4_scale_tiles"].data_ptr(), tl["int4_zp_tiles"].data_ptr(), st_)
+    ms = _time_ms(_tiles)
+    b = n + n // 128 * 2 * 2 + n // 2 + n // 128 * 4 * 2
+    res["c5_int4_tiles_from_stored_Wt"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
+                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
     for m in (1, 4, 16):
         A = torch.randn(m, 8192, generator=g, device=dev).to(torch.bfloat16)
         ms = _time_ms(lambda: bb.linear(A, sw, out_dtype=torch.bfloat16), iters=50)

@@ -16,7 +16,9 @@ from .types import (  # noqa: F401
     MXFP8BlockScaling, NVFP4BlockScaling, INT4Scaling,
     Layout, PerTensor, PerBlockK, PerChannel, PerBlockMN,
 )
-from .api import cast, dequantize, requantize, matmul, linear, gemm_operands  # noqa: F401
+from .api import (cast, dequantize, requantize, matmul, linear, gemm_operands,  # noqa: F401
+                  attach_gemm_operands)
+from . import bridges  # noqa: F401
 from .autograd import cast_ste, cast_ste_clipped  # noqa: F401
 from .plugin import install, uninstall  # noqa: F401
 

@@ -37,6 +37,11 @@ PROTOTYPES = {
     "brc_cast_int4": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "brc_cast_ste_pertensor_fp8": ([_p, _i, _i64, _i, _p, _p, _p], _i),
     "brc_cast_ste_block": ([_p, _i, _i64, _i64, _i, _i, _i, _i, _i, _i, _p, _p], _i),
+    "brc_pack_nibbles_hi": ([_p, _i64, _p, _p], _i),
+    "brc_unpack_nibbles_hi": ([_p, _i64, _p, _p, _p], _i),
+    "brc_pack_codes_lo": ([_p, _i64, _p, _p], _i),
+    "brc_scale_atoms": ([_p, _i64, _i64, _p, _p], _i),
+    "brc_int4_tiles": ([_p, _i64, _i64, _p, _p, _i, _p, _p, _p, _p], _i),
     "brc_dequant_pertensor_fp8": ([_p, _i64, _i, _p, _p, _i, _p], _i),
     "brc_dequant_block_fp8": ([_p, _i64, _i64, _i, _i, _i, _p, _p, _i, _p], _i),
     "brc_dequant_mxfp8": ([_p, _i64, _i64, _i, _p, _p, _i, _p], _i),

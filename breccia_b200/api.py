@@ -34,7 +34,8 @@ import torch
 from . import _lib
 from . import types as T
 
-__all__ = ["cast", "dequantize", "requantize", "matmul", "linear", "gemm_operands"]
+__all__ = ["cast", "dequantize", "requantize", "matmul", "linear", "gemm_operands",
+           "attach_gemm_operands"]
 
 _TORCH_FP8 = {"E4M3": torch.float8_e4m3fn, "E5M2": torch.float8_e5m2}
 _FMT = {"E4M3": _lib.FP8_E4M3, "E5M2": _lib.FP8_E5M2}
@@ -353,6 +354,61 @@ def linear(a, w, out_dtype=torch.bfloat16):
     block-scaled tensor-core GEMMs consume directly."""
     from . import gemm
     return gemm.linear(a, w, _torch_out_dtype(out_dtype))
+
+
+def attach_gemm_operands(scaled):
+    """Rebuild, on the GPU, the side operands ``cast`` records for the
+    tensor-core GEMMs, for a CUDA ``ScaledTensor`` that was not cast here
+    (loaded from a file, or produced by another implementation): for NVFP4
+    the packed codes (tensor-core nibble order) and the tcgen05 scale atoms,
+    for MXFP8 the scale atoms, for INT4 of group 128 with a multiple of 16
+    rows the skinny-GEMM tiles. They equal what ``cast`` writes byte for
+    byte, so ``matmul`` / ``linear`` take the same kernels. Other recipes
+    need none. Returns ``scaled``."""
+    name = getattr(getattr(scaled, "recipe", None), "name", None)
+    data = scaled.data
+    if name not in ("nvfp4", "mxfp8", "int4") or not isinstance(data, torch.Tensor) \
+            or not data.is_cuda or data.ndim < 1:
+        return scaled
+    side = _side(data)
+    dev = data.device
+    codes = _aligned(data.contiguous().view(torch.uint8))
+    K = codes.shape[-1]
+    rows = codes.numel() // K if K else 0
+    if rows == 0:
+        return scaled
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        if name in ("nvfp4", "mxfp8"):
+            add = {}
+            bs = 16 if name == "nvfp4" else 32
+            if "sf_mma" not in side:
+                sc = _aligned(scaled.scale.contiguous().view(torch.uint8))
+                sf = torch.empty(_mma_scale_shape(rows, K // bs), dtype=torch.uint8, device=dev)
+                _lib.call("brc_scale_atoms", sc.data_ptr(), rows, K // bs, sf.data_ptr(), st)
+                add["sf_mma"] = sf
+            if name == "nvfp4" and "packed" not in side and K % 2 == 0:
+                packed = torch.empty(codes.shape[:-1] + (K // 2,), dtype=torch.uint8, device=dev)
+                _lib.call("brc_pack_codes_lo", codes.data_ptr(), codes.numel(),
+                          packed.data_ptr(), st)
+                add["packed"] = packed
+            if add:
+                _remember(data, **add)
+        elif "int4_tiles" not in side and scaled.recipe.group_size == 128 and \
+                rows % 16 == 0 and K % 128 == 0:
+            sc = _aligned(scaled.scale.contiguous())
+            if sc.dtype not in (torch.float16, torch.float32):
+                return scaled
+            sdt = _lib.SCALE_F16 if sc.dtype == torch.float16 else _lib.SCALE_F32
+            zp = None if scaled.zero_point is None else \
+                _aligned(scaled.zero_point.contiguous().to(sc.dtype))
+            tiles = torch.empty(rows * K // 2, dtype=torch.uint8, device=dev)
+            stiles = torch.empty(rows * (K // 128), dtype=torch.float32, device=dev)
+            ztiles = None if zp is None else torch.empty_like(stiles)
+            _lib.call("brc_int4_tiles", codes.data_ptr(), rows, K, sc.data_ptr(), _ptr(zp),
+                      sdt, tiles.data_ptr(), stiles.data_ptr(), _ptr(ztiles), st)
+            _remember(data, int4_tiles=tiles, int4_scale_tiles=stiles, int4_zp_tiles=ztiles)
+    return scaled
 
 
 def gemm_operands(scaled) -> dict:

@@ -160,6 +160,39 @@ int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int gr
                   uint8_t* packed, void* scales, void* zero_points, uint8_t* packed_tiles,
                   float* scale_tiles, float* zp_tiles, void* stream);
 
+/* ======================================================= stored 4-bit data, GEMM operands
+ * breccia's on-disk nibble order puts element 2i in the HIGH nibble of byte i
+ * (src/breccia/_formats.py:227-243 pack_nibbles, 246-260 unpack_nibbles); the
+ * tensor cores read element 2i from the LOW nibble. Codes are one per byte in
+ * the low nibble (the reference's ScaledTensor.data for NVFP4 and INT4).
+ * n: number of codes, even. codes 16-byte aligned; packed buffers 8-byte
+ * aligned.
+ * brc_pack_nibbles_hi:   packed[i] = codes[2i] << 4 | codes[2i+1] (pack_nibbles).
+ * brc_unpack_nibbles_hi: codes[2i] = packed[i] >> 4, codes[2i+1] = packed[i]
+ *                        & 15 (unpack_nibbles), and/or the same pairs in the
+ *                        tensor-core order into packed_lo (either may be NULL).
+ * brc_pack_codes_lo:     packed_lo[i] = codes[2i] | codes[2i+1] << 4 (the
+ *                        "packed" operand brc_cast_nvfp4 writes). */
+int brc_pack_nibbles_hi(const uint8_t* codes, int64_t n, uint8_t* packed, void* stream);
+int brc_unpack_nibbles_hi(const uint8_t* packed, int64_t n, uint8_t* codes, uint8_t* packed_lo,
+                          void* stream);
+int brc_pack_codes_lo(const uint8_t* codes, int64_t n, uint8_t* packed_lo, void* stream);
+/* The tcgen05 scale-factor atoms (the sf_mma layout brc_cast_mxfp8 /
+ * brc_cast_nvfp4 write) from stored one-byte scales (rows, scale_cols): MXFP8
+ * E8M0 or NVFP4 E4M3 codes (cast.py:420-446, 468-496). atoms holds
+ * ceil(rows/128) * ceil(scale_cols/4) * 512 bytes, every one written (padding
+ * zero), 4-byte aligned. */
+int brc_scale_atoms(const uint8_t* scales, int64_t rows, int64_t scale_cols, uint8_t* atoms,
+                    void* stream);
+/* The INT4 skinny-GEMM tiles brc_cast_int4 writes (packed_tiles, scale_tiles,
+ * zp_tiles; layout in brc_cast_int4's comment) from a stored INT4 tensor of
+ * group 128: codes (rows, cols) one per byte, scales and zero_points (rows,
+ * cols/128) in scale_dtype (zero_points and zp_tiles both NULL when
+ * symmetric) (cast.py:516-571). rows % 16 == 0, cols % 128 == 0. */
+int brc_int4_tiles(const uint8_t* codes, int64_t rows, int64_t cols, const void* scales,
+                   const void* zero_points, int scale_dtype, uint8_t* tiles, float* scale_tiles,
+                   float* zp_tiles, void* stream);
+
 /* ======================================================= cast_ste (fused)
  * The forward value of breccia.autograd.cast_ste / cast_ste_clipped for one
  * recipe in a single pass: out = x + (dequantize(cast(x, recipe)) - x) in
