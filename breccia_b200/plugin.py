@@ -4,10 +4,13 @@ breccia has no registry: its public functions are plain module attributes
 (``src/breccia/__init__.py:23`` re-exports ``cast, dequantize, requantize,
 matmul`` from ``breccia.kernels.reference`` and ``__init__.py:24``
 ``cast_ste, cast_ste_clipped`` from ``breccia.autograd``;
-``breccia/autograd.py:47`` imports ``cast`` and ``dequantize`` by name). ``install()`` rebinds each of
-those names to a wrapper that sends CUDA torch inputs to breccia_b200 and
-calls breccia's original function for everything else (NumPy, CPU torch,
-JAX, MLX). ``uninstall()`` restores the originals.
+``breccia/autograd.py:47`` imports ``cast`` and ``dequantize`` by name; the
+safetensors bridge is ``breccia.bridges.save_safetensors`` /
+``load_safetensors``). ``install()`` rebinds each of those names to a wrapper
+that sends CUDA torch inputs (and the bridge's ``pack_4bit`` / ``device``
+extensions) to breccia_b200 and calls breccia's original function for
+everything else (NumPy, CPU torch, JAX, MLX). ``uninstall()`` restores the
+originals.
 """
 
 from __future__ import annotations
@@ -21,6 +24,8 @@ _SITES = [
     ("breccia.kernels.reference.cast", ("cast", "dequantize", "requantize")),
     ("breccia.kernels.reference.matmul", ("dequantize",)),
     ("breccia.autograd", ("cast", "dequantize", "cast_ste", "cast_ste_clipped")),
+    ("breccia.bridges", ("save_safetensors", "load_safetensors")),
+    ("breccia.bridges._huggingface", ("save_safetensors", "load_safetensors")),
 ]
 _saved: dict = {}
 
@@ -34,12 +39,26 @@ def _on_cuda(obj) -> bool:
 
 
 def _wrap(name, original):
-    from . import api, autograd
+    from . import api, autograd, bridges
 
-    ours = getattr(autograd if name.startswith("cast_ste") else api, name)
+    if name.endswith("_safetensors"):
+        ours = getattr(bridges, name)
+    else:
+        ours = getattr(autograd if name.startswith("cast_ste") else api, name)
 
     @functools.wraps(original)
     def dispatch(*args, **kwargs):
+        if name == "save_safetensors":
+            # CUDA tensors and the packed format here; NumPy / CPU data on breccia's bridge
+            tensors = args[0] if args else kwargs.get("scaled_tensors", {})
+            if kwargs.get("pack_4bit") or any(_on_cuda(st) for st in dict(tensors).values()):
+                return ours(*args, **kwargs)
+            return original(*args, **kwargs)
+        if name == "load_safetensors":
+            # device= (loading onto the GPU) is this backend's; plain loads stay breccia's
+            if kwargs.get("device") is not None:
+                return ours(*args, **kwargs)
+            return original(*args, **kwargs)
         if name == "matmul":
             a, b = args[0], args[1]
             if _on_cuda(a) or _on_cuda(b):
@@ -56,7 +75,12 @@ def install() -> None:
     """Route breccia's cast/dequantize/requantize/matmul for CUDA tensors to
     this backend. Idempotent."""
     for modname, names in _SITES:
-        mod = importlib.import_module(modname)
+        try:
+            mod = importlib.import_module(modname)
+        except ImportError:
+            if modname.startswith("breccia.bridges"):
+                continue  # the bridges are optional in a stripped breccia install
+            raise
         for name in names:
             fn = getattr(mod, name, None)
             if fn is None or getattr(fn, "__breccia_b200__", False):

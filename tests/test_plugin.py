@@ -35,6 +35,12 @@ def fake_breccia(monkeypatch):
                 setattr(m, fn, mk(f"{modname}.{fn}"))
         mods[modname] = m
         monkeypatch.setitem(sys.modules, modname, m)
+    for modname in ("breccia.bridges", "breccia.bridges._huggingface"):
+        m = types.ModuleType(modname)
+        for fn in ("save_safetensors", "load_safetensors"):
+            setattr(m, fn, mk(f"{modname}.{fn}"))
+        mods[modname] = m
+        monkeypatch.setitem(sys.modules, modname, m)
     yield mods, calls
     plugin.uninstall()
 
@@ -64,6 +70,28 @@ def test_install_rebinds_cast_ste(fake_breccia):
             assert f(np.zeros((2, 32), np.float32), None) == f"{modname}.{fn}"
     plugin.uninstall()
     assert mods["breccia"].cast_ste(np.zeros(1), None) == "breccia.cast_ste"
+
+
+def test_install_routes_bridges(fake_breccia, tmp_path):
+    """Plain saves / loads keep breccia's bridge; CUDA tensors, pack_4bit and
+    device= come here."""
+    mods, calls = fake_breccia
+    breccia_b200.install()
+    for modname in ("breccia.bridges", "breccia.bridges._huggingface"):
+        save, load = mods[modname].save_safetensors, mods[modname].load_safetensors
+        assert getattr(save, "__breccia_b200__", False)
+        cpu_st = breccia_b200.ScaledTensor(data=torch.zeros(2, 32, dtype=torch.uint8),
+                                           scale=torch.ones(2, 2), recipe=breccia_b200.NVFP4BlockScaling(),
+                                           layout=breccia_b200.PerBlockMN(1, 16))
+        path = str(tmp_path / "x.safetensors")
+        assert save({"w": cpu_st}, path) == f"{modname}.save_safetensors"
+        assert load(path) == f"{modname}.load_safetensors"
+        with pytest.raises(TypeError, match="CUDA"):  # ours: packing needs CUDA tensors
+            save({"w": cpu_st}, path, pack_4bit=True)
+        with pytest.raises(TypeError, match="CUDA device"):  # ours
+            load(path, device="cpu")
+    plugin.uninstall()
+    assert not getattr(mods["breccia.bridges"].save_safetensors, "__breccia_b200__", False)
 
 
 def test_cuda_check_without_gpu():
