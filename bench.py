@@ -619,8 +619,9 @@ def per_recipe(peaks, src):
     atoms_ = torch.empty(bb.gemm_operands(sw)["sf_mma"].numel(), dtype=torch.uint8, device=dev)
 
     def _load_nvfp4():
-        L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes_.data_ptr(), lo_.data_ptr(), st_)
-        L.call("brc_scale_atoms", sw.scale.data_ptr(), 28672, 8192 // 16, atoms_.data_ptr(), st_)
+        s_ = torch.cuda.current_stream().cuda_stream  # the capturing stream under a graph
+        L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes_.data_ptr(), lo_.data_ptr(), s_)
+        L.call("brc_scale_atoms", sw.scale.data_ptr(), 28672, 8192 // 16, atoms_.data_ptr(), s_)
     ms = _time_ms(_load_nvfp4)
     b = n // 2 + n // 16 + n + n // 2 + atoms_.numel()
     res["c4_load_Wt_nvfp4_from_packed"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
@@ -640,7 +641,8 @@ def per_recipe(peaks, src):
     def _tiles():
         L.call("brc_int4_tiles", sw.data.data_ptr(), 28672, 8192, sw.scale.data_ptr(),
                sw.zero_point.data_ptr(), L.SCALE_F16, tl["int4_tiles"].data_ptr(),
-               tl["int4_scale_tiles"].data_ptr(), tl["int4_zp_tiles"].data_ptr(), st_)
+               tl["int4_scale_tiles"].data_ptr(), tl["int4_zp_tiles"].data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
     ms = _time_ms(_tiles)
     b = n + n // 128 * 2 * 2 + n // 2 + n // 128 * 4 * 2
     res["c5_int4_tiles_from_stored_Wt"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,

@@ -68,28 +68,32 @@ __global__ void __launch_bounds__(kThreads) k_pack(const uint8_t* __restrict__ c
   }
 }
 
-// 8 packed bytes (high-first) -> 16 codes and/or 8 bytes in the tensor-core order.
+// 16 packed bytes (high-first) -> 32 codes and/or 16 bytes in the tensor-core
+// order per thread step (packed and packed_lo 16-byte aligned on this path).
 __global__ void __launch_bounds__(kThreads) k_unpack_hi(const uint8_t* __restrict__ packed,
                                                         int64_t n, uint8_t* __restrict__ codes,
                                                         uint8_t* __restrict__ packed_lo) {
-  const int64_t nv = n / 16;
+  const int64_t nv = n / 32;
   for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < nv;
        i += (int64_t)gridDim.x * kThreads) {
-    const uint2 p = *reinterpret_cast<const uint2*>(packed + 8 * i);
-    const uint32_t pw[2] = {p.x, p.y};
-    uint32_t cw[4], lw[2];
+    const uint4 p = *reinterpret_cast<const uint4*>(packed + 16 * i);
+    const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+    uint32_t cw[8], lw[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < 4; ++h) {
       const uint32_t hi = (pw[h] >> 4) & 0x0F0F0F0Fu;  // elements 0, 2, 4, 6
       const uint32_t lo = pw[h] & 0x0F0F0F0Fu;         // elements 1, 3, 5, 7
       cw[2 * h] = prmt(hi, lo, 0x5140u);               // 0, 1, 2, 3
       cw[2 * h + 1] = prmt(hi, lo, 0x7362u);           // 4, 5, 6, 7
       lw[h] = hi | (lo << 4);
     }
-    if (codes) *reinterpret_cast<uint4*>(codes + 16 * i) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-    if (packed_lo) *reinterpret_cast<uint2*>(packed_lo + 8 * i) = make_uint2(lw[0], lw[1]);
+    if (codes) {
+      *reinterpret_cast<uint4*>(codes + 32 * i) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+      *reinterpret_cast<uint4*>(codes + 32 * i + 16) = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+    }
+    if (packed_lo) *reinterpret_cast<uint4*>(packed_lo + 16 * i) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  const int64_t done = nv * 16;
+  const int64_t done = nv * 32;
   for (int64_t j = done / 2 + blockIdx.x * (int64_t)kThreads + threadIdx.x; j < n / 2;
        j += (int64_t)gridDim.x * kThreads) {
     const uint32_t b = packed[j];
@@ -129,9 +133,9 @@ __global__ void __launch_bounds__(kThreads) k_scale_atoms(const uint8_t* __restr
 }
 
 // INT4 skinny-GEMM tiles (group 128, rows % 16 == 0) from stored codes, one
-// thread per 8-element run: tile (r / 16) * groups + g, row r % 16 at
+// thread per two 8-element runs: tile (r / 16) * groups + g, row r % 16 at
 // 64 * (r % 16), byte 4j + i = element 8j + i | element 8j + i + 4 << 4; the
-// run-0 thread of each (row, group) also writes the float32 scale and
+// first thread of each (row, group) also writes the float32 scale and
 // 128 + zero point at tile * 16 + 2 * (r % 8) + (r % 16) / 8.
 template <bool F16>
 __global__ void __launch_bounds__(kThreads) k_int4_tiles(
@@ -139,17 +143,18 @@ __global__ void __launch_bounds__(kThreads) k_int4_tiles(
     const void* __restrict__ zp, uint8_t* __restrict__ tiles, float* __restrict__ scale_tiles,
     float* __restrict__ zp_tiles) {
   const int64_t groups = cols / 128;
-  const int64_t runs = rows * groups * 16;
-  for (int64_t t = blockIdx.x * (int64_t)kThreads + threadIdx.x; t < runs;
+  const int64_t pairs = rows * groups * 8;  // pairs of 8-element runs
+  for (int64_t t = blockIdx.x * (int64_t)kThreads + threadIdx.x; t < pairs;
        t += (int64_t)gridDim.x * kThreads) {
-    const int64_t row = t / (groups * 16);
-    const int64_t rem = t - row * groups * 16;
-    const int64_t g = rem >> 4;
-    const int j = (int)(rem & 15);
-    const uint2 c = *reinterpret_cast<const uint2*>(codes + row * cols + 128 * g + 8 * j);
-    const uint32_t a = c.x & 0x0F0F0F0Fu, b = c.y & 0x0F0F0F0Fu;
+    const int64_t row = t / (groups * 8);
+    const int64_t rem = t - row * groups * 8;
+    const int64_t g = rem >> 3;
+    const int j = 2 * (int)(rem & 7);  // first run of the pair
+    const uint4 c = *reinterpret_cast<const uint4*>(codes + row * cols + 128 * g + 8 * j);
     const int64_t tile = (row >> 4) * groups + g;
-    *reinterpret_cast<uint32_t*>(tiles + tile * 1024 + (row & 15) * 64 + 4 * j) = a | (b << 4);
+    *reinterpret_cast<uint2*>(tiles + tile * 1024 + (row & 15) * 64 + 4 * j) =
+        make_uint2((c.x & 0x0F0F0F0Fu) | ((c.y & 0x0F0F0F0Fu) << 4),
+                   (c.z & 0x0F0F0F0Fu) | ((c.w & 0x0F0F0F0Fu) << 4));
     if (j == 0) {
       const int64_t q = tile * 16 + (row & 7) * 2 + ((row >> 3) & 1);
       const int64_t si = row * groups + g;
@@ -199,10 +204,9 @@ int brc_unpack_nibbles_hi(const uint8_t* packed, int64_t n, uint8_t* codes, uint
   if (n < 0 || n % 2) return BRC_ERR_SHAPE;
   if (n == 0) return BRC_OK;
   if (!packed || (!codes && !packed_lo)) return BRC_ERR_NULL;
-  if ((reinterpret_cast<uintptr_t>(packed) & 7u) || (codes && !al16(codes)) ||
-      (packed_lo && (reinterpret_cast<uintptr_t>(packed_lo) & 7u)))
+  if (!al16(packed) || (codes && !al16(codes)) || (packed_lo && !al16(packed_lo)))
     return BRC_ERR_ALIGN;
-  k_unpack_hi<<<grid_for(n / 16 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
+  k_unpack_hi<<<grid_for(n / 32 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
                                                                             packed_lo);
   return check_launch();
 }
@@ -230,14 +234,14 @@ int brc_int4_tiles(const uint8_t* codes, int64_t rows, int64_t cols, const void*
   if ((zero_points == nullptr) != (zp_tiles == nullptr)) return BRC_ERR_NULL;
   if (scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32) return BRC_ERR_DTYPE;
   if (!al16(codes) || !al16(tiles)) return BRC_ERR_ALIGN;
-  const int64_t runs = rows * (cols / 128) * 16;
+  const int64_t pairs = rows * (cols / 128) * 8;
   cudaStream_t st = (cudaStream_t)stream;
   if (scale_dtype == BRC_SCALE_F16)
-    k_int4_tiles<true><<<grid_for(runs), kThreads, 0, st>>>(codes, rows, cols, scales,
+    k_int4_tiles<true><<<grid_for(pairs), kThreads, 0, st>>>(codes, rows, cols, scales,
                                                             zero_points, tiles, scale_tiles,
                                                             zp_tiles);
   else
-    k_int4_tiles<false><<<grid_for(runs), kThreads, 0, st>>>(codes, rows, cols, scales,
+    k_int4_tiles<false><<<grid_for(pairs), kThreads, 0, st>>>(codes, rows, cols, scales,
                                                              zero_points, tiles, scale_tiles,
                                                              zp_tiles);
   return check_launch();

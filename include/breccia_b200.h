@@ -166,7 +166,7 @@ int brc_cast_int4(const void* x, int x_dtype, int64_t rows, int64_t cols, int gr
  * tensor cores read element 2i from the LOW nibble. Codes are one per byte in
  * the low nibble (the reference's ScaledTensor.data for NVFP4 and INT4).
  * n: number of codes, even. codes 16-byte aligned; packed buffers 8-byte
- * aligned.
+ * aligned (16-byte for brc_unpack_nibbles_hi).
  * brc_pack_nibbles_hi:   packed[i] = codes[2i] << 4 | codes[2i+1] (pack_nibbles).
  * brc_unpack_nibbles_hi: codes[2i] = packed[i] >> 4, codes[2i+1] = packed[i]
  *                        & 15 (unpack_nibbles), and/or the same pairs in the
