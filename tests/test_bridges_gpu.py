@@ -202,3 +202,19 @@ def test_load_reference_file_onto_gpu():
     assert "sf_mma" in bb.gemm_operands(gpu["mxfp8"])
     assert "int4_tiles" in bb.gemm_operands(gpu["int4_asym"])
     assert "int4_tiles" in bb.gemm_operands(gpu["int4_sym"])
+
+
+def test_dlpack_zero_copy_of_outputs():
+    """The reference's DLPack bridge (src/breccia/bridges/_dlpack.py:18-67)
+    hands this backend's CUDA outputs on without copying: torch's DLPack
+    export carries the float8 dtypes, and consumers without float8 take the
+    uint8 view of the same bytes."""
+    import breccia_b200 as bb
+    x = torch.randn(64, 256, device="cuda")
+    for r in (bb.Float8CurrentScaling(), bb.MXFP8BlockScaling(), bb.NVFP4BlockScaling()):
+        st = bb.cast(x, r)
+        for t in (st.data, st.scale):
+            back = torch.from_dlpack(t.__dlpack__())
+            assert back.data_ptr() == t.data_ptr() and back.dtype == t.dtype
+        u8 = torch.from_dlpack(st.data.view(torch.uint8))
+        assert u8.data_ptr() == st.data.data_ptr()
