@@ -291,6 +291,39 @@ def test_int4_gemm_tile_layout(symmetric):
                                       128.0 + st.zero_point.float().cpu().numpy())
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_nvfp4_quotients_near_midpoints(dtype):
+    """NVFP4 blocks whose quotients x / s sit on and within a few ulps of every
+    E2M1 midpoint, for non-power-of-two E4M3 scales (in about a third of them
+    x * RN(1/s) differs from RN(x / s)): the codes must follow the IEEE
+    quotient, as the oracle's division does, bit for bit."""
+    from oracle import cast as ocast
+    from breccia_b200.types import NVFP4BlockScaling
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    rows = []
+    for k in range(-12, 7):
+        for mant in (1.125, 1.25, 1.375, 1.625, 1.875, 1.0):
+            s = np.float32(mant * 2.0 ** k)
+            for d in range(-6, 7):
+                # one element 6 s fixes the block scale at s; 15 elements near midpoints
+                vals = [np.float32(6.0) * s]
+                for i in range(15):
+                    x = mids[i % 7] * s
+                    x = np.float32(x)
+                    step = np.inf if d > 0 else -np.inf
+                    for _ in range(abs(d) + (i // 7)):
+                        x = np.nextafter(x, np.float32(step))
+                    vals.append(x if i % 2 == 0 else -x)
+                rows.append(vals)
+    x = np.array(rows, np.float32).reshape(-1, 48)  # 1482 blocks, three per row
+    if dtype == torch.bfloat16:
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    r = NVFP4BlockScaling()
+    st = bb().cast(torch.from_numpy(x).to(dtype).cuda(), r)
+    q = ocast.cast(x, r)
+    assert_cast_equal(st, q)
+
+
 def test_division_matches_ieee():
     from breccia_b200 import _lib
     g = torch.Generator().manual_seed(5)
