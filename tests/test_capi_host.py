@@ -90,3 +90,33 @@ def test_call_raises_python_exceptions():
         _lib.call("brc_cast_block_fp8", p, 5, 4, 128, 128, 0, p, p, None)
     with pytest.raises(_lib.BrecciaB200Error):
         _lib.call("brc_cast_block_fp8", None, 0, 4, 128, 128, 0, p, p, None)
+
+
+def test_bridge_entry_points_reject_bad_arguments():
+    """Stored-4-bit / operand-rebuild entry points: shape, null, alignment and
+    dtype checks happen on the host, before any CUDA call."""
+    L = _lib.lib()
+    _, p = _buf(256)
+    # odd code counts, negative sizes
+    assert L.brc_pack_nibbles_hi(p, 3, p, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_unpack_nibbles_hi(p, -2, p, None, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_pack_codes_lo(p, 5, p, None) == _lib.BRC_ERR_SHAPE
+    # empty inputs are a no-op
+    assert L.brc_pack_nibbles_hi(None, 0, None, None) == _lib.BRC_OK
+    assert L.brc_scale_atoms(None, 0, 8, None, None) == _lib.BRC_OK
+    assert L.brc_int4_tiles(None, 0, 128, None, None, 0, None, None, None, None) == _lib.BRC_OK
+    # null buffers
+    assert L.brc_pack_nibbles_hi(None, 4, p, None) == _lib.BRC_ERR_NULL
+    assert L.brc_unpack_nibbles_hi(p, 4, None, None, None) == _lib.BRC_ERR_NULL
+    assert L.brc_scale_atoms(None, 4, 4, p, None) == _lib.BRC_ERR_NULL
+    assert L.brc_int4_tiles(p, 16, 128, None, None, 0, p, p, None, None) == _lib.BRC_ERR_NULL
+    # zero points and their tiles come together
+    assert L.brc_int4_tiles(p, 16, 128, p, p, 0, p, p, None, None) == _lib.BRC_ERR_NULL
+    # alignment
+    assert L.brc_pack_nibbles_hi(p + 1, 4, p, None) == _lib.BRC_ERR_ALIGN
+    assert L.brc_unpack_nibbles_hi(p + 8, 4, p, None, None) == _lib.BRC_ERR_ALIGN
+    assert L.brc_scale_atoms(p, 4, 4, p + 2, None) == _lib.BRC_ERR_ALIGN
+    # shapes the INT4 tile layout cannot hold, and scale dtypes it does not take
+    assert L.brc_int4_tiles(p, 15, 128, p, None, 0, p, p, None, None) == _lib.BRC_ERR_UNSUPPORTED
+    assert L.brc_int4_tiles(p, 16, 96, p, None, 0, p, p, None, None) == _lib.BRC_ERR_UNSUPPORTED
+    assert L.brc_int4_tiles(p, 16, 128, p, None, 7, p, p, None, None) == _lib.BRC_ERR_DTYPE
