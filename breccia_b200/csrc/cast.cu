@@ -950,6 +950,46 @@ __device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ uint32_t h2min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// 2^k in both halves of an f16x2 (k in [-14, 15], a normal f16).
+__device__ __forceinline__ uint32_t f16x2_pow2(int k) {
+  const uint32_t h = (uint32_t)(k + 15) << 10;
+  return h | (h << 16);
+}
+
+// Four MXFP8 codes of four f16 values (h0 = elements 0, 1; h1 = elements 2, 3)
+// that are scaled by m1 * m2 (powers of two) before encoding. The f16 values
+// are exact products, and so are their scaled values wherever these reach the
+// format's first midpoint (see k_requant_nv_to_mx). As the float32 encoders
+// do with float32 bits, the code is read off the scaled f16 bits: E4M3 scales
+// carry an extra 2^-8 that puts E4M3's smallest normal (2^-6) on f16's
+// (2^-14), E5M2's smallest normal is f16's; clamp to the format maximum
+// (np.clip; an f16 overflow to inf clamps too), add half-1 below the code bits
+// and truncate (ties toward zero). A zero magnitude drops its sign.
+template <int FMT>
+__device__ __forceinline__ uint32_t enc4_fp8_from_f16x2(uint32_t h0, uint32_t h1, uint32_t m1,
+                                                        uint32_t m2, bool two_steps) {
+  constexpr uint32_t kMaxH = FMT == BRC_FP8_E4M3 ? 0x3F003F00u    // 448 * 2^-8 = 1.75
+                                                 : 0x7B007B00u;   // 57344
+  constexpr uint32_t kRnd = FMT == BRC_FP8_E4M3 ? 0x003F003Fu : 0x007F007Fu;
+  constexpr int kDrop = FMT == BRC_FP8_E4M3 ? 7 : 8;  // f16 mantissa bits below the code
+  uint32_t v0 = h2mul(h0 & 0x7FFF7FFFu, m1), v1 = h2mul(h1 & 0x7FFF7FFFu, m1);
+  if (two_steps) {
+    v0 = h2mul(v0, m2);
+    v1 = h2mul(v1, m2);
+  }
+  v0 = h2min(v0, kMaxH);
+  v1 = h2min(v1, kMaxH);
+  const uint32_t c0 = ((v0 + kRnd) >> kDrop) & 0x007F007Fu;  // codes in bytes 0 and 2
+  const uint32_t c1 = ((v1 + kRnd) >> kDrop) & 0x007F007Fu;
+  const uint32_t w = prmt(c0, c1, 0x6420u);
+  const uint32_t neg = prmt(h0, h1, 0xFDB9u);  // sign of each f16 replicated into its byte
+  return apply_sign8(w, neg);
+}
 
 template <int FMT>
 __global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restrict__ codes,
@@ -986,21 +1026,34 @@ __global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restr
       const uint32_t row = fdiv((uint32_t)blk, bpr);
       out_mma[sf_mma_offset(row, (uint32_t)blk - row * bpr.d, sf_col_tiles)] = (uint8_t)e;
     }
-    float f[32];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const __half2 v = *reinterpret_cast<const __half2*>(&h[i]);
-      f[2 * i] = __low2float(v);
-      f[2 * i + 1] = __high2float(v);
-    }
     uint32_t o[8];
     if (isfinite(am)) {
-      const float inv = exp2i(127 - (int)e);
+      // Exactness of the f16 route. Each product y = decode(code) * decode(scale)
+      // has at most 6 significant bits and is 0 or lies in [2^-10, 2688], so the
+      // f16 h[] hold y exactly. The scaled value y * 2^(127 - e) (* 2^-8 for
+      // E4M3) is exact wherever it is at least the format's first midpoint (f16
+      // subnormals step by 2^-24, which 6 bits from 2^-18 up never need), and
+      // below that midpoint the code is 0 however it rounds. 2^k is applied in
+      // at most two steps of f16 powers of two (E4M3: k in [-11, 11]; E5M2: k in
+      // [0, 26]); a value that overflows f16 lies above the format maximum and
+      // clamps to it, as np.clip does.
+      // (a block whose products are all 0 has am at the 1e-10 floor and a larger
+      // k; its codes are 0 under any finite multiplier, so k is capped at 30)
+      const int k = min(127 - (int)e - (FMT == BRC_FP8_E4M3 ? 8 : 0), 30);
+      const int k1 = k > 15 ? 15 : k;
+      const uint32_t m1 = f16x2_pow2(k1), m2 = f16x2_pow2(k - k1);
+      const bool two = k != k1;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        o[j] = enc4_fp8<FMT>(__fmul_rn(f[4 * j], inv), __fmul_rn(f[4 * j + 1], inv),
-                             __fmul_rn(f[4 * j + 2], inv), __fmul_rn(f[4 * j + 3], inv));
+        o[j] = enc4_fp8_from_f16x2<FMT>(h[2 * j], h[2 * j + 1], m1, m2, two);
     } else {
+      float f[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const __half2 v = *reinterpret_cast<const __half2*>(&h[i]);
+        f[2 * i] = __low2float(v);
+        f[2 * i + 1] = __high2float(v);
+      }
       const float act = e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {

@@ -324,6 +324,37 @@ def test_nvfp4_quotients_near_midpoints(dtype):
     assert_cast_equal(st, q)
 
 
+@pytest.mark.parametrize("fmt", ["E4M3", "E5M2"])
+def test_requant_nvfp4_to_mxfp8_adversarial(fmt):
+    """The fused NVFP4 -> MXFP8 requantize on hand-built NVFP4 tensors: random
+    E2M1 codes under every finite E4M3 scale code (subnormals included), MXFP8
+    blocks whose two NVFP4 halves have extreme scale ratios, all-zero blocks,
+    zero scales, and NaN scales (the non-finite path). Codes and E8M0 scales
+    bit-exact against the oracle's cast(dequantize(st))."""
+    from oracle import cast as ocast
+    from breccia_b200.types import NVFP4BlockScaling, MXFP8BlockScaling, PerBlockMN
+    rng = np.random.default_rng(3 if fmt == "E4M3" else 4)
+    rows, K = 512, 256
+    codes = rng.integers(0, 16, (rows, K), dtype=np.uint8)
+    sc = rng.integers(0, 0x7F, (rows, K // 16), dtype=np.uint8)  # finite E4M3 codes
+    sc[0, :] = np.arange(K // 16, dtype=np.uint8) * 7              # a sweep of codes
+    sc[1, 0::2], sc[1, 1::2] = 1, 0x7E                             # 2^-9 next to 448
+    sc[2, 0::2], sc[2, 1::2] = 0x7E, 1
+    sc[3, :] = 0                                                    # zero scales
+    codes[4, :] = 0                                                 # all-zero codes
+    codes[5, :] = 8                                                 # negative zeros
+    sc[6, 3] = 0x7F                                                 # NaN scale
+    sc[7, :] = np.arange(1, 1 + K // 16, dtype=np.uint8)            # subnormal scales
+    r_src, r_dst = NVFP4BlockScaling(), MXFP8BlockScaling(fp8_format=fmt)
+    st = bb().ScaledTensor(data=torch.from_numpy(codes).cuda(), scale=torch.from_numpy(sc).cuda(),
+                           recipe=r_src, layout=PerBlockMN(block_m=1, block_n=16))
+    got = bb().requantize(st, r_dst)
+    q = ocast.Q(codes, sc, ("per_block_mn", 1, 16), r_src)
+    want = ocast.cast(ocast.dequantize(q), r_dst)
+    assert same_bits(_np(got.data), want.data), _first_diff(_np(got.data), want.data)
+    assert same_bits(_np(got.scale), want.scale), _first_diff(_np(got.scale), want.scale)
+
+
 def test_division_matches_ieee():
     from breccia_b200 import _lib
     g = torch.Generator().manual_seed(5)
