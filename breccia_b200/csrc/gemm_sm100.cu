@@ -14,7 +14,7 @@
 //
 // One persistent CTA per SM, 10 warps:
 //   warp 0    TMA producer (operand tiles + scale atoms) into a 4-stage ring
-//   warp 1    TMEM owner and MMA issuer (one thread)
+//   warp 1    TMEM owner and MMA warp (the whole warp runs the loop, lane 0 issues)
 //   warps 2-9 epilogue: each pulls 128 accumulator columns of 32 rows from
 //             TMEM into registers, releases the accumulator, then scales,
 //             converts and stores while the next tile's MMAs run.
@@ -263,30 +263,38 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA warp
+    // The whole warp runs the loop, so addresses and descriptors stay
+    // warp-uniform; lane 0 issues the copies, MMAs and every commit (a commit
+    // tracks the tcgen05 operations of the thread that issues it). Run by one
+    // lane inside a divergent branch, the loop's per-stage cost made the MMA
+    // thread the bound of the block-FP8 GEMM.
+    {
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
+      const uint32_t a_base = smem_u32(smem + L::kA), b_base = smem_u32(smem + L::kB);
+      const uint64_t dhi = desc_sw128_hi();
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, abort_flag, p.status, 1u)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(tmem_empty, acc_phase ^ 1u, abort_flag, p.status, 1u))) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, p.status, 1u))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + L::kB + stage * B_BYTES);
+          const uint32_t alo = desc_sw128_lo(a_base + stage * A_BYTES);
+          const uint32_t blo = desc_sw128_lo(b_base + stage * B_BYTES);
           uint32_t sfa_col = 0, sfb_col = 0;
           if constexpr (kCopier) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
-            if (!mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u)) {
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u))) {
               ok = false;
               break;
             }
@@ -294,61 +302,73 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
-            const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
-            const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
-#pragma unroll
-            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-              tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-              tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-              tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
-            }
           }
+          if (lane == 0) {
+            if constexpr (!kCopier && KIND != kPerTensor) {
+              const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
+              const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
 #pragma unroll
-          for (uint32_t k = 0; k < 4; ++k) {
-            const uint64_t ad = desc_kmajor_sw128(a_addr + 32 * k);
-            const uint64_t bd = desc_kmajor_sw128(b_addr + 32 * k);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if constexpr (KIND == kPerTensor) {
-              mma_f8f6f4(tmem + ACC_COL, ad, bd, idesc_f8f6f4(AFMT, BFMT, BM, BN), acc);
-            } else if constexpr (KIND == kMxfp8) {
-              mma_mxf8f6f4(tmem + ACC_COL, ad, bd,
-                           idesc_block_scaled(AFMT, BFMT, BM, BN, 1u, k, k),
-                           sfa_col | (k << 30), sfb_col | (k << 30), acc);
-            } else {
-              mma_mxf4nvf4_4x(tmem + ACC_COL, ad, bd, idesc_block_scaled(1u, 1u, BM, BN, 0u, 0u, 0u),
-                              sfa_col + 4 * k, sfb_col + 8 * k, acc);
+              for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+                tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+                tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+                tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+              }
             }
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+              const uint64_t ad = dhi | (uint64_t)(alo + 2 * k);
+              const uint64_t bd = dhi | (uint64_t)(blo + 2 * k);
+              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+              if constexpr (KIND == kPerTensor) {
+                mma_f8f6f4(tmem + ACC_COL, ad, bd, idesc_f8f6f4(AFMT, BFMT, BM, BN), acc);
+              } else if constexpr (KIND == kMxfp8) {
+                mma_mxf8f6f4(tmem + ACC_COL, ad, bd,
+                             idesc_block_scaled(AFMT, BFMT, BM, BN, 1u, k, k),
+                             sfa_col | (k << 30), sfb_col | (k << 30), acc);
+              } else {
+                mma_mxf4nvf4_4x(tmem + ACC_COL, ad, bd,
+                                idesc_block_scaled(1u, 1u, BM, BN, 0u, 0u, 0u), sfa_col + 4 * k,
+                                sfb_col + 8 * k, acc);
+              }
+            }
+            tc_commit(&empty[stage]);
+            if constexpr (kCopier) tc_commit(&sf_free[stage]);
           }
-          tc_commit(&empty[stage]);
-          if constexpr (kCopier) tc_commit(&sf_free[stage]);
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(tmem_full);
+        if (lane == 0) tc_commit(tmem_full);
+        __syncwarp();
         acc_phase ^= 1u;
       }
-      // every MMA this thread issued has completed before TMEM is freed
-      tc_commit(drain);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      // every MMA lane 0 issued has completed before TMEM is freed
+      if (lane == 0) {
+        tc_commit(drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+        }
       }
+      __syncwarp();
     }
   } else if (kCopier && warp == 2 + kEpiWarps) {
     // ------------------------------------------------------------ scale-factor copier
     // Copies each stage's scale atoms from shared memory into that stage's
     // TMEM slot once the stage has landed and the MMAs that read the slot
     // last have completed; its commit tells the MMA thread the slot is ready.
-    if (lane == 0) {
+    // The whole warp runs the loop; lane 0 issues the copies and commits.
+    {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) ||
-              !mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+          const bool w = mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) &&
+                         mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u);
+          if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
           }
@@ -357,24 +377,30 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           const uint32_t sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
           const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
           const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
+          if (lane == 0) {
 #pragma unroll
-          for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-            tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-            tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-            tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+              tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+              tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+              tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+            }
+            tc_commit(&sf_full[stage]);
           }
-          tc_commit(&sf_full[stage]);
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // every copy this thread issued has completed before TMEM is freed
-      tc_commit(cdrain);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      // every copy lane 0 issued has completed before TMEM is freed
+      if (lane == 0) {
+        tc_commit(cdrain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+        }
       }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -591,32 +617,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (leader)
-    if (rank == 0 && lane == 0) {
+    // ------------------------------------------------------------ MMA warp (leader)
+    // As in the single-CTA kernel: the whole warp runs the loop with
+    // warp-uniform addresses and descriptors; lane 0 issues the copies, MMAs
+    // and every commit.
+    if (rank == 0) {
       int stage = 0, abuf = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
+      const uint32_t a_base = smem_u32(smem + C::kA), b_base = smem_u32(smem + C::kB);
+      const uint64_t dhi = desc_sw128_hi();
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         // accumulator buffer abuf: free once both CTAs' epilogues read it
-        if (!mbar_wait(&tmem_empty[abuf], acc_phase ^ 1u, abort_flag, p.status, 1u)) {
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(&tmem_empty[abuf], acc_phase ^ 1u, abort_flag, p.status, 1u))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t dacc = tmem + 256u * abuf;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, p.status, 1u))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + C::kA + stage * P_A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + C::kB + stage * P_B_BYTES);
+          const uint32_t alo = desc_sw128_lo(a_base + stage * P_A_BYTES);
+          const uint32_t blo = desc_sw128_lo(b_base + stage * P_B_BYTES);
           uint32_t sfa_col = 0, sfb_col = 0;
           if constexpr (kCopier) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
-            if (!mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u)) {
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&sf_full[stage], phase, abort_flag, p.status, 1u))) {
               ok = false;
               break;
             }
@@ -624,64 +657,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
-            const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
-            const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
-#pragma unroll
-            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-              tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-              tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-              tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
-            }
           }
+          if (lane == 0) {
+            if constexpr (!kCopier && KIND != kPerTensor) {
+              const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
+              const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
 #pragma unroll
-          for (uint32_t k = 0; k < 4; ++k) {
-            const uint64_t ad = desc_kmajor_sw128(a_addr + 32 * k);
-            const uint64_t bd = desc_kmajor_sw128(b_addr + 32 * k);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if constexpr (KIND == kPerTensor) {
-              mma_f8f6f4_pair(dacc, ad, bd, idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN), acc);
-            } else if constexpr (KIND == kMxfp8) {
-              mma_mxf8f6f4_pair(dacc, ad, bd, idesc_block_scaled(AFMT, BFMT, P_BM, P_BN, 1u, k, k),
-                                sfa_col | (k << 30), sfb_col | (k << 30), acc);
-            } else {
-              mma_mxf4nvf4_4x_pair(dacc, ad, bd,
-                                   idesc_block_scaled(1u, 1u, P_BM, P_BN, 0u, 0u, 0u),
-                                   sfa_col + 4 * k, sfb_col + 8 * k, acc);
+              for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+                tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+                tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+                tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+              }
             }
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+              const uint64_t ad = dhi | (uint64_t)(alo + 2 * k);
+              const uint64_t bd = dhi | (uint64_t)(blo + 2 * k);
+              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+              if constexpr (KIND == kPerTensor) {
+                mma_f8f6f4_pair(dacc, ad, bd, idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN), acc);
+              } else if constexpr (KIND == kMxfp8) {
+                mma_mxf8f6f4_pair(dacc, ad, bd,
+                                  idesc_block_scaled(AFMT, BFMT, P_BM, P_BN, 1u, k, k),
+                                  sfa_col | (k << 30), sfb_col | (k << 30), acc);
+              } else {
+                mma_mxf4nvf4_4x_pair(dacc, ad, bd,
+                                     idesc_block_scaled(1u, 1u, P_BM, P_BN, 0u, 0u, 0u),
+                                     sfa_col + 4 * k, sfb_col + 8 * k, acc);
+              }
+            }
+            tc_commit_pair(&empty[stage], 0x3);
+            if constexpr (kCopier) tc_commit_pair(&sf_free[stage], 0x1);
           }
-          tc_commit_pair(&empty[stage], 0x3);
-          if constexpr (kCopier) tc_commit_pair(&sf_free[stage], 0x1);
+          __syncwarp();
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(&tmem_full[abuf], 0x3);
+        if (lane == 0) tc_commit_pair(&tmem_full[abuf], 0x3);
+        __syncwarp();
         if (++abuf == C::kNacc) {
           abuf = 0;
           acc_phase ^= 1u;
         }
       }
-      // every MMA issued has completed before the pair frees TMEM
-      tc_commit_pair(drain, 0x1);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      // every MMA lane 0 issued has completed before the pair frees TMEM
+      if (lane == 0) {
+        tc_commit_pair(drain, 0x1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+        }
       }
+      __syncwarp();
     }
   } else if (kCopier && warp == 2 + kEpiWarps) {
     // ------------------------------------------------------------ scale-factor copier (leader)
     // The leader's full barrier counts both CTAs' copies, so once it completes
     // both CTAs' scale atoms of the stage are in shared memory; each
     // tcgen05.cp cta_group::2 moves every CTA's atoms into its own TMEM.
-    if (rank == 0 && lane == 0) {
+    // The whole warp runs the loop; lane 0 issues the copies and commits.
+    if (rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) ||
-              !mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
+          const bool w = mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) &&
+                         mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u);
+          if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
           }
@@ -690,24 +735,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           const uint32_t sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
           const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
           const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
+          if (lane == 0) {
 #pragma unroll
-          for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-            tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-            tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-            tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+            for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
+              tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
+              tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
+              tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+            }
+            tc_commit_pair(&sf_full[stage], 0x1);
           }
-          tc_commit_pair(&sf_full[stage], 0x1);
+          __syncwarp();
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // every copy issued has completed before the pair frees TMEM
-      tc_commit_pair(cdrain, 0x1);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      // every copy lane 0 issued has completed before the pair frees TMEM
+      if (lane == 0) {
+        tc_commit_pair(cdrain, 0x1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+        }
       }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -853,28 +904,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // MMA warp: the whole warp runs the loop with warp-uniform addresses and
+    // descriptors; lane 0 issues the MMAs and every commit.
+    {
       int stage = 0, pbuf = 0;
       uint32_t phase = 0, pphase = 0;
       bool ok = true;
       const uint32_t idesc = idesc_f8f6f4(AFMT, BFMT, BM, BN);
+      const uint32_t a_base = smem_u32(smem + L::kA), b_base = smem_u32(smem + L::kB);
+      const uint64_t dhi = desc_sw128_hi();
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&pempty[pbuf], pphase ^ 1u, abort_flag, p.status, 1u) ||
-              !mbar_wait(&full[stage], phase, abort_flag, p.status, 1u)) {
+          const bool w = mbar_wait(&pempty[pbuf], pphase ^ 1u, abort_flag, p.status, 1u) &&
+                         mbar_wait(&full[stage], phase, abort_flag, p.status, 1u);
+          if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + L::kB + stage * B_BYTES);
+          const uint32_t alo = desc_sw128_lo(a_base + stage * A_BYTES);
+          const uint32_t blo = desc_sw128_lo(b_base + stage * B_BYTES);
           const uint32_t d = tmem + pbuf * kPartialCols;
+          if (lane == 0) {
 #pragma unroll
-          for (uint32_t k = 0; k < 4; ++k)
-            mma_f8f6f4(d, desc_kmajor_sw128(a_addr + 32 * k), desc_kmajor_sw128(b_addr + 32 * k),
-                       idesc, k > 0 ? 1u : 0u);
-          tc_commit(&empty[stage]);
-          tc_commit(&pfull[pbuf]);
+            for (uint32_t k = 0; k < 4; ++k)
+              mma_f8f6f4(d, dhi | (uint64_t)(alo + 2 * k), dhi | (uint64_t)(blo + 2 * k), idesc,
+                         k > 0 ? 1u : 0u);
+            tc_commit(&empty[stage]);
+            tc_commit(&pfull[pbuf]);
+          }
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -883,10 +942,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (pbuf == 0) pphase ^= 1u;
         }
       }
-      tc_commit(drain);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+      if (lane == 0) {
+        tc_commit(drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
+        }
       }
+      __syncwarp();
     }
   } else {
     const int ew = warp - 2;

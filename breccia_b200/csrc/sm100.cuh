@@ -256,6 +256,17 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
   return smem_desc(saddr, 16, 1024, 2);
 }
+// The same descriptor in two words: the high word (stride, version, swizzle)
+// is one constant, the low word holds the start address (>> 4) and the
+// leading-offset field. MMA loops build the high word once and step only the
+// low word (+2 per 32-byte K step); shared addresses are below 256 KB, so the
+// 14-bit address field never carries into the offset field.
+__device__ __forceinline__ uint64_t desc_sw128_hi() {
+  return desc_kmajor_sw128(0u) & 0xFFFFFFFF00000000ull;
+}
+__device__ __forceinline__ uint32_t desc_sw128_lo(uint32_t saddr) {
+  return static_cast<uint32_t>(desc_kmajor_sw128(saddr));
+}
 // Scale-factor atom for tcgen05.cp 32x128b: 8-row x 16-byte core matrices
 // stacked along M every 128 bytes, no swizzle.
 __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
