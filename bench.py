@@ -46,10 +46,10 @@ WORKLOAD = ("C2 Float8CurrentScaling E4M3 per-tensor: A bf16 (16384, 8192) N(0,1
 METRIC = "scaled-matmul TFLOP/s (C2 per-tensor FP8: cast A + cast W + GEMM, whole job)"
 
 # DRAM bytes (read + write) of one launch of the GEMM kernel on this
-# workload, from one ncu capture of `bench.py --steps 2 --warmup 3 --no-e2e
-# --no-cpu-baseline` (dram__bytes_read.sum 663.62 MB + dram__bytes_write.sum
-# 246.02 MB; profiles/gemm_fp8_pertensor_c2.txt).
-GEMM_DRAM_BYTES = 663.62e6 + 246.02e6
+# workload, from one ncu capture of `bench.py --steps 1 --warmup 3 --no-e2e
+# --no-cpu-baseline` (dram__bytes_read.sum 679.50 MB + dram__bytes_write.sum
+# 248.64 MB; profiles/gemm_fp8_pertensor_c2.md).
+GEMM_DRAM_BYTES = 679.50e6 + 248.64e6
 
 
 def parse():
@@ -428,7 +428,7 @@ def run_ours(args):
     achieved = gemm_flops_rank / (gemm_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_fp8, "unit": "TFLOP/s",
                 "frac": achieved / peak_fp8, "traffic": GEMM_DRAM_BYTES,
-                "kernel": "brc::gemm::k_gemm<kPerTensor,E4M3,E4M3,bf16>",
+                "kernel": "brc::gemm::k_gemm_pair<kPerTensor,E4M3,E4M3,bf16>",
                 "peak_source": f"2 x bf16_tflops_sustained of {src} MEASURED_PEAKS.json "
                                "(dense FP8 = 2x dense bf16)",
                 "frac_vs_burst": achieved / (2.0 * peaks["bf16_tflops"]),
