@@ -821,9 +821,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
 // Each epilogue warp owns one 128-column half of the tile, so its B scale is
 // one value per K block.
 constexpr uint32_t kPartialCols = 256;
+// 12 warps: warp 0 producer, warp 1 MMA, warps 2-3 idle, warps 4-11 promotion
+// and epilogue. The first warpgroup gives up registers (setmaxnreg) so that
+// each promotion thread holds its 128 accumulators and two 32-column TMEM
+// loads in flight: 384 threads x 168 registers at launch = 128 x 56 + 256 x 224.
+constexpr int kBlockThreads = 32 * (4 + kEpiWarps);
+constexpr uint32_t kBlockCtlRegs = 56, kBlockEpiRegs = 224, kBlockLaunchRegs = 168;
+static_assert(128 * kBlockCtlRegs + 32 * kEpiWarps * kBlockEpiRegs <=
+                  kBlockThreads * kBlockLaunchRegs,
+              "register split must fit the launch allocation");
+static_assert(kBlockLaunchRegs * kBlockThreads <= 65536 &&
+                  65536 / kBlockThreads / 8 * 8 == kBlockLaunchRegs,
+              "launch bounds give 168 registers per thread");
 
 template <int AFMT, int BFMT, int OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
     k_gemm_block(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b, const Params p) {
   using L = Smem<kPerTensor>;
@@ -868,7 +880,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_sh;
-
+  if (warp < 4) {
+  regs_dec<kBlockCtlRegs>();
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
@@ -950,8 +963,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
+  }  // warps 2-3: nothing to do
   } else {
-    const int ew = warp - 2;
+    regs_inc<kBlockEpiRegs>();
+    const int ew = warp - 4;
     const int quad = warp & 3;
     const int half = ew / 4;
     int pbuf = 0;
@@ -982,17 +997,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + pbuf * kPartialCols + 128 * half;
+        // 32-column TMEM loads, one in flight while the previous one is
+        // promoted; the partial buffer is handed back once the last load has
+        // landed, before its FMAs. Packed FMAs (fma.rn.f32x2) round each
+        // element as one IEEE fma.
+        const float2 s2 = make_float2(s, s);
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr, ra);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t ra[16];
-          tmem_ld16(taddr + 16 * c, ra);
-          tmem_ld_wait16(ra);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+          tmem_ld_wait();
+          reg_bind32(cur);
+          if (c < 3) {
+            tmem_ld32(taddr + 32 * (c + 1), nxt);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pempty[pbuf]);
+          }
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 * c + i] = __fmaf_rn(__uint_as_float(ra[i]), s, acc[16 * c + i]);
+          for (int i = 0; i < 16; ++i) {
+            const float2 v = __ffma2_rn(
+                make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), s2,
+                make_float2(acc[32 * c + 2 * i], acc[32 * c + 2 * i + 1]));
+            acc[32 * c + 2 * i] = v.x;
+            acc[32 * c + 2 * i + 1] = v.y;
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[pbuf]);
         pbuf ^= 1;
         if (pbuf == 0) pphase ^= 1u;
       }
@@ -1142,7 +1175,7 @@ int launch_block(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   }
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kBlockThreads, smem, st>>>(ta, tb, p);
   return check_launch();
 }
 

@@ -235,6 +235,33 @@ __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Names 32 registers written by an earlier tcgen05.ld; placed after
+// tmem_ld_wait() (volatile asm keeps the order), it keeps every use of them
+// below the wait.
+__device__ __forceinline__ void reg_bind32(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
+
+// ----------------------------------------------------------------- registers
+// Per-warpgroup register budget (setmaxnreg; every warp of the warpgroup
+// executes it). An increase is granted from the registers the CTA was
+// launched with (threads x registers per thread at launch), so the callers'
+// budgets must add up to no more than that total, or the increase never
+// completes.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // ----------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor: start address (>>4) in bits [0,14), leading
