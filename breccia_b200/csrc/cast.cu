@@ -725,9 +725,10 @@ __global__ void __launch_bounds__(kB2dThreads, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   const int tile_bytes = bm * 128 * elem_bytes<DT>();
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)stages * tile_bytes);
-  float* red = reinterpret_cast<float*>(full + stages);  // one value per warp
-  float* s_sh = red + kB2dThreads / 32;
-  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(s_sh + 1);
+  // per-warp maxima, two sets used by alternate tiles
+  float* red = reinterpret_cast<float*>(full + stages);
+  volatile uint32_t* abort_flag =
+      reinterpret_cast<volatile uint32_t*>(red + 2 * (kB2dThreads / 32));
   const int64_t tiles_c = cols / 128;
   const int64_t ntiles = tiles_c * (rows / bm);
   const int nvec = bm * VPR;
@@ -771,22 +772,23 @@ __global__ void __launch_bounds__(kB2dThreads, 1)
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    float* red_j = red + (j & 1) * (kB2dThreads / 32);
+    if ((threadIdx.x & 31) == 0) red_j[threadIdx.x >> 5] = m;
     if (__syncthreads_or(!ok)) {  // also: every thread has read stage s
       aborted = true;
       break;
     }
     const int64_t t = blockIdx.x + j * gridDim.x;
-    if (threadIdx.x == 0) {
-      if (issued < my_tiles && !*abort_flag) issue();
-      float a = red[0];
-      for (int w = 1; w < kB2dThreads / 32; ++w) a = fmax_nan(a, red[w]);
-      const float sc = __fdiv_rn(fmax_nan(a, 1e-10f), kMax);
-      *s_sh = sc;
-      scales[t] = canon_nan(sc);
-    }
-    __syncthreads();
-    const float sc = *s_sh;
+    if (threadIdx.x == 0 && issued < my_tiles && !*abort_flag) issue();
+    // Every thread reduces the per-warp maxima itself (the max is
+    // order-independent, NaN included), so no second barrier waits on one
+    // thread. A set is rewritten two tiles later, after a barrier that every
+    // thread reaches only once it has read the set.
+    float a = red_j[0];
+#pragma unroll
+    for (int w = 1; w < kB2dThreads / 32; ++w) a = fmax_nan(a, red_j[w]);
+    const float sc = __fdiv_rn(fmax_nan(a, 1e-10f), kMax);
+    if (threadIdx.x == 0) scales[t] = canon_nan(sc);
     const float r = __frcp_rn(sc);
     uint8_t* cbase = codes + (t / tiles_c) * bm * cols + (t % tiles_c) * 128;
     if (isfinite(sc)) {
@@ -1273,7 +1275,7 @@ struct Block2d {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
       });
       const int tile_bytes = bm * 128 * elem_bytes<DT>();
-      const int extra = 16 * 8 + (kB2dThreads / 32 + 1) * 4 + 16;
+      const int extra = 16 * 8 + 2 * (kB2dThreads / 32) * 4 + 16;
       int stages = (kSmemMax - extra) / tile_bytes;
       if (stages > 6) stages = 6;
       if (stages >= 2) {
