@@ -149,11 +149,13 @@ def test_tensor_core_path_is_taken():
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 256), (256, 512, 1024), (200, 384, 768),
-                                   (2048, 4096, 7168)])
+                                   (2048, 4096, 7168), (384, 512, 128), (1000, 1280, 384)])
 @pytest.mark.parametrize("fmt", ["E4M3", "E5M2"])
 def test_block_fp8_deepseek(M, N, K, fmt):
     """Float8BlockScaling: 1 x 128 activation scales, 128 x 128 weight scales
-    (restated oracle for the weight layout; the reference cannot produce it)."""
+    (restated oracle for the weight layout; the reference cannot produce it).
+    Includes a single K block (K = 128) and an odd number of K blocks, so the
+    two partial buffers are used unevenly."""
     from oracle import cast as ocast
     from breccia_b200 import gemm
     from breccia_b200.types import Float8BlockScaling
