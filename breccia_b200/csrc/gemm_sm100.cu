@@ -12,7 +12,8 @@
 // Block scales are consumed in the 512-byte "atom" layout the casts write
 // (128 rows x 4 scale columns per atom).
 //
-// One persistent CTA per SM, 10 warps:
+// One persistent CTA per SM, 10 warps (11 with the scale-factor copier; the
+// block-FP8 kernel has its own 12-warp layout, described there):
 //   warp 0    TMA producer (operand tiles + scale atoms) into a 4-stage ring
 //   warp 1    TMEM owner and MMA warp (the whole warp runs the loop, lane 0 issues)
 //   warps 2-9 epilogue: each pulls 128 accumulator columns of 32 rows from
@@ -52,7 +53,7 @@ constexpr int STAGES = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 // Single-CTA block-scaled GEMMs add one warp that copies the scale atoms
-// into TMEM (tcgen05.cp), so the copies are issued beside the MMA thread
+// into TMEM (tcgen05.cp), so the copies are issued beside the MMA warp
 // rather than between its MMAs.
 constexpr bool kSfCopier = true;
 template <int KIND>
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
     // ------------------------------------------------------------ scale-factor copier
     // Copies each stage's scale atoms from shared memory into that stage's
     // TMEM slot once the stage has landed and the MMAs that read the slot
-    // last have completed; its commit tells the MMA thread the slot is ready.
+    // last have completed; its commit tells the MMA warp the slot is ready.
     // The whole warp runs the loop; lane 0 issues the copies and commits.
     {
       int stage = 0;
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
 // rows of B^T (its half of the tile's N) into its own shared memory, so a
 // stage is ~32 KB per CTA and the ring is 5-7 deep (the single-CTA kernel
 // moves 48 KB per stage through a 4-deep ring). Both CTAs' copies complete
-// on the leader's (rank 0's) "full" barrier, the leader's single MMA thread
+// on the leader's (rank 0's) "full" barrier, lane 0 of the leader's MMA warp
 // issues M = 256 MMAs, and their commits reach both CTAs' "empty" and
 // accumulator barriers; both CTAs' epilogue warps release the accumulator on
 // the leader's barrier. Block-scaled kinds: each CTA also stages the scale
