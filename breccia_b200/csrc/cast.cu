@@ -182,8 +182,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
         const float r = __frcp_rn(s);
 #pragma unroll
         for (int j = 0; j < NW; ++j)
-          w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
-                               div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+          w[j] = enc4_div<enc4p_fp8<FMT>>(f + 4 * j, s, r);
       }
     } else {
 #pragma unroll
@@ -204,8 +203,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
       const float r = __frcp_rn(s);
 #pragma unroll
       for (int j = 0; j < NW; ++j)
-        w[j] = enc4_e2m1(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
-                         div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+        w[j] = enc4_div<enc4p_e2m1>(f + 4 * j, s, r);
     } else {
 #pragma unroll
       for (int j = 0; j < NW; ++j) {
@@ -683,8 +681,7 @@ __global__ void __launch_bounds__(256) k_block2d_cast(const void* __restrict__ x
         uint32_t w[V / 4];
 #pragma unroll
         for (int j = 0; j < V / 4; ++j)
-          w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
-                               div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+          w[j] = enc4_div<enc4p_fp8<FMT>>(f + 4 * j, s, r);
         store_words<V / 4>(codes + offset(k), w);
       }
     }
@@ -801,8 +798,7 @@ __global__ void __launch_bounds__(kB2dThreads, 1)
           uint32_t w[V / 4];
 #pragma unroll
           for (int q = 0; q < V / 4; ++q)
-            w[q] = enc4_fp8<FMT>(div_by(f[4 * q], sc, r), div_by(f[4 * q + 1], sc, r),
-                                 div_by(f[4 * q + 2], sc, r), div_by(f[4 * q + 3], sc, r));
+            w[q] = enc4_div<enc4p_fp8<FMT>>(f + 4 * q, sc, r);
           store_words<V / 4>(cbase + (int64_t)(idx / VPR) * cols + (idx % VPR) * V, w);
         }
       }

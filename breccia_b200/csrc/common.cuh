@@ -128,6 +128,21 @@ __device__ __forceinline__ float div_by(float x, float s, float r) {
   return __fmaf_rn(e, r, q);
 }
 __device__ __forceinline__ float div_ieee(float x, float s) { return __fdiv_rn(x, s); }
+// Four quotients f[i] / s in two packed pairs (mul.rn.f32x2 and fma.rn.f32x2
+// round each element exactly as the scalar instructions do): the same three
+// roundings per element as div_by, in half the FMA-pipe instructions.
+__device__ __forceinline__ void div4(const float* f, float s, float r, float* q) {
+  const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float2 x = make_float2(f[2 * h], f[2 * h + 1]);
+    const float2 t = __fmul2_rn(x, r2);
+    const float2 e = __ffma2_rn(t, ns2, x);  // x - t*s, one rounding
+    const float2 y = __ffma2_rn(e, r2, t);
+    q[2 * h] = y.x;
+    q[2 * h + 1] = y.y;
+  }
+}
 
 // IEEE x / d for a constant d with rd = RN(1/d): Markstein's step for finite
 // x (the callers' x are amax values floored at 1e-10, so the quotient is a
@@ -230,10 +245,60 @@ __device__ __forceinline__ uint32_t enc4_e2m1(float a, float b, float c, float d
   return apply_sign4(w, sign_bytes(a, b, c, d));
 }
 
+// Packed forms of the encoders above (same codes): the round-up scaling of the
+// *_mag_hi encoders two values per packed multiply (mul.ru.f32x2), then the
+// same bit step. They halve the FMA-pipe work of instruction-bound casts
+// (NVFP4, the 2-D block cast); an HBM-bound pass (the per-tensor encode)
+// measured 5% slower with them, so the scalar forms remain: SHIFT and the (half - 1)
+// addend are the encoders' (4 / 0x007FFFF0 E4M3, 3 / 0x007FFFF8 E5M2,
+// 2 / 0x007FFFFC E2M1).
+template <int SHIFT, uint32_t ADD>
+__device__ __forceinline__ uint32_t enc4_mag(float ma, float mb, float mc, float md,
+                                             float factor) {
+  const float2 f2 = make_float2(factor, factor);
+  const float2 t01 = __fmul2_ru(make_float2(ma, mb), f2);
+  const float2 t23 = __fmul2_ru(make_float2(mc, md), f2);
+  return pack_top_bytes((__float_as_uint(t01.x) << SHIFT) + ADD,
+                        (__float_as_uint(t01.y) << SHIFT) + ADD,
+                        (__float_as_uint(t23.x) << SHIFT) + ADD,
+                        (__float_as_uint(t23.y) << SHIFT) + ADD);
+}
+__device__ __forceinline__ uint32_t enc4p_e4m3(float a, float b, float c, float d) {
+  const uint32_t w = enc4_mag<4, 0x007FFFF0u>(fminf(fabsf(a), 448.f), fminf(fabsf(b), 448.f),
+                                             fminf(fabsf(c), 448.f), fminf(fabsf(d), 448.f),
+                                             0x1p-120f);
+  return apply_sign8(w, sign_bytes(a, b, c, d));
+}
+__device__ __forceinline__ uint32_t enc4p_e5m2(float a, float b, float c, float d) {
+  const uint32_t w = enc4_mag<3, 0x007FFFF8u>(fminf(fabsf(a), 57344.f), fminf(fabsf(b), 57344.f),
+                                             fminf(fabsf(c), 57344.f), fminf(fabsf(d), 57344.f),
+                                             0x1p-112f);
+  return apply_sign8(w, sign_bytes(a, b, c, d));
+}
+__device__ __forceinline__ uint32_t enc4p_e2m1(float a, float b, float c, float d) {
+  const uint32_t w = enc4_mag<2, 0x007FFFFCu>(fminf(fabsf(a), 6.f), fminf(fabsf(b), 6.f),
+                                             fminf(fabsf(c), 6.f), fminf(fabsf(d), 6.f),
+                                             0x1p-126f);
+  return apply_sign4(w, sign_bytes(a, b, c, d));
+}
+
 template <int FMT>
 __device__ __forceinline__ uint32_t enc4_fp8(float a, float b, float c, float d) {
   if constexpr (FMT == BRC_FP8_E4M3) return enc4_e4m3(a, b, c, d);
   else return enc4_e5m2(a, b, c, d);
+}
+template <int FMT>
+__device__ __forceinline__ uint32_t enc4p_fp8(float a, float b, float c, float d) {
+  if constexpr (FMT == BRC_FP8_E4M3) return enc4p_e4m3(a, b, c, d);
+  else return enc4p_e5m2(a, b, c, d);
+}
+// Encode f[0..3] / s (r = RN(1/s)) with one of the four-value encoders:
+// quotients and scaling both in packed pairs.
+template <uint32_t (*ENC)(float, float, float, float)>
+__device__ __forceinline__ uint32_t enc4_div(const float* f, float s, float r) {
+  float q[4];
+  div4(f, s, r, q);
+  return ENC(q[0], q[1], q[2], q[3]);
 }
 
 // Single-value encoders with full NaN / inf handling (scale paths and the
