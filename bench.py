@@ -6,19 +6,39 @@ Headline workload (Float8CurrentScaling E4M3):
   W bf16 (8192, 8192) ~ N(0,0.02), held as W^T (N, K) (nn.Linear orientation).
   One step = per-tensor cast of A + per-tensor cast of W^T + the 16384 x 8192 x
   8192 tcgen05 FP8 GEMM -> bf16.
-  N GPUs, default (--shard batch, data parallel, "weak" scaling): every rank
-  holds its own batch of 16384 activation rows (rank 0's is the C2 A above,
-  the others are seeded per rank) and the whole weight. The activations'
-  per-tensor scale is that of the concatenated global batch (16384*N rows):
-  one NCCL all-reduce(MAX) of a 4-byte amax word, overlapped with the
-  weight's cast. Per-GPU work is fixed as N grows.
-  --shard weight ("strong" scaling): W^T is split along N (rows); the
-  weight's amax is reduced with one all-reduce; A is replicated; each rank
-  computes its C[:, shard]. Total work is fixed.
 
-value = total 2*M*N*K over all ranks / step time (max over ranks).
+  N GPUs, default (--shard weight, "strong" scaling): W^T is split along N into 128-aligned row blocks, one per rank; A is
+  replicated. Each rank reduces 1/N of A's rows and its W^T shard into two
+  amax words, ONE NCCL all-reduce(MAX) of those 8 bytes gives both global
+  amaxes, then each rank encodes all of A and its shard and computes its
+  C[:, n0:n1]. Total work is fixed as N grows; the replicated A encode is the
+  part that does not shrink.
+  --shard batch ("weak" scaling): every rank holds its own batch of 16384
+  activation rows and the whole weight; one all-reduce(MAX) of the
+  activations' amax word, overlapped with the weight's cast.
+
+value = total 2*M*N*K over all ranks / step time (max over ranks), device-timed
+        with the inputs resident in HBM.
 e2e   = the same through the public API with the inputs copied from pinned
-        host memory and the output C copied back inside every step.
+        host memory and C copied back inside every step.
+
+Further objects on the line:
+  parity     sampled rows x columns of the headline's own output C against the
+             CPU oracle (the reference's dequantize-then-float32 matmul).
+  roofline   the headline GEMM kernel against dense FP8 = 2 x the measured
+             burst bf16 peak (the timed region is well under a second).
+  sharded    the N-sharded configs (C2 GEMM; C3 MXFP8 and C4 NVFP4 weight casts
+             and GEMMs; C5 INT4 weight cast and M = 1/4/16 GEMVs), each timed on
+             every rank and reported as whole-job throughput over the max rank
+             time, with the replicated activation casts reported separately.
+  per_recipe (N = 1) every BASELINE config at full size: cast, dequantize and
+             requantize GB/s and GEMM / GEMV TFLOP/s, each with its fraction of
+             the measured burst peaks; inputs rotated so that every launch reads
+             data not left in L2 by the previous one.
+  library_reference (N = 1) cuBLASLt's scaled GEMMs (torch.nn.functional
+             .scaled_mm) on the same operands, a same-box FP8/FP4 reference
+             point outside the product path, each checked against our output.
+  cpu_baseline (N = 1, rank 0) the CPU oracle port on a bounded sample.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 Under torchrun one process per GPU; rank 0 prints one JSON line.
@@ -31,7 +51,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -44,11 +63,13 @@ WORKLOAD = ("C2 Float8CurrentScaling E4M3 per-tensor: A bf16 (16384, 8192) N(0,1
             "N(0,1)*50 outliers, W bf16 (8192, 8192) N(0,0.02) held as W^T; cast A + cast W "
             "+ 16384x8192x8192 tcgen05 FP8 GEMM -> bf16")
 METRIC = "scaled-matmul TFLOP/s (C2 per-tensor FP8: cast A + cast W + GEMM, whole job)"
+L2_BYTES = 126e6
 
-# DRAM bytes (read + write) of one launch of the GEMM kernel on this
-# workload, from one ncu capture of `bench.py --steps 1 --warmup 3 --no-e2e
-# --no-cpu-baseline` (dram__bytes_read.sum 679.50 MB + dram__bytes_write.sum
-# 248.64 MB; profiles/gemm_fp8_pertensor_c2.md).
+# DRAM bytes (read + write) of one launch of the headline GEMM on one GPU,
+# from one ncu capture of `bench.py --steps 1 --warmup 3 --no-e2e
+# --no-cpu-baseline --no-per-recipe --no-sharded` (dram__bytes_read.sum
+# 679.50 MB + dram__bytes_write.sum 248.64 MB). Reported as the roofline's
+# `traffic` with its source; it is not measured inside this run.
 GEMM_DRAM_BYTES = 679.50e6 + 248.64e6
 
 
@@ -58,19 +79,35 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--shard", default="batch", choices=["batch", "weight"],
-                    help="N>1 layout: per-rank activation batches with the weight replicated "
-                         "(weak scaling, default) or the weight split along N (strong)")
+    ap.add_argument("--shard", default="weight", choices=["weight", "batch"],
+                    help="N>1 layout: W^T split along N with A replicated (strong scaling, "
+                         "default) or per-rank activation batches with W replicated (weak)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--per-recipe", action="store_true",
-                    help="also measure every BASELINE config's cast GB/s and GEMM TFLOP/s")
+    ap.add_argument("--no-per-recipe", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of A / W^T the CPU port encodes per sample (default 64 for "
                          "cpu_baseline, 16 per step for --impl reference)")
     ap.add_argument("--ncu-case", default=None, choices=sorted(NCU_CASES),
                     help="run one kernel on a small case (inputs > L2, < 1 GB) 3 times, for ncu")
     return ap.parse_args()
+
+
+def headline_config(world, shard):
+    """The `config` object of the line; the reference arm prints the same."""
+    batch = shard == "batch" and world > 1
+    return {"workload": WORKLOAD, "M": M * (world if batch else 1), "N": N, "K": K,
+            "M_per_gpu": M,
+            "parallelism": "single GPU" if world == 1 else
+            (f"data parallel over {world} GPUs: {M} activation rows per GPU, W replicated, "
+             "one NCCL all-reduce(MAX) of the activations' amax (overlapped with the weight "
+             "cast)") if batch else
+            (f"W^T split along N over {world} GPUs ({N // world} rows each), A replicated; "
+             "one NCCL all-reduce(MAX) of two amax words (1/N of A's rows and the W shard "
+             "per rank)"),
+            "l2": "inputs larger than L2 (A is 268 MB)"}
 
 
 # --------------------------------------------------------------- CPU side
@@ -95,7 +132,7 @@ def cpu_reference_step(A_np, Wt_np, rows, pool, nproc):
 
     Returns (seconds for the whole step, breakdown dict)."""
     import numpy as np
-    from oracle import codec, cast as ocast
+    from oracle import codec
 
     t = {}
     t0 = time.perf_counter()
@@ -135,14 +172,14 @@ def run_reference(args):
     """--impl reference: the oracle port of breccia's NumPy path on the host.
     Each step is a bounded sample (16 rows of A and of W^T encoded, about a
     second of host time) extrapolated to the whole C2 step, so the run stays
-    within minutes for any --steps / --warmup the driver passes."""
+    within minutes for any --steps / --warmup the driver passes. Under
+    torchrun only rank 0 runs and prints; the other ranks exit at once."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     if args.cpu_rows is None:
         args.cpu_rows = 16
     import multiprocessing as mp
-    import numpy as np
     from concurrent.futures import ProcessPoolExecutor
     A_np, Wt_np = host_inputs_numpy()
     nproc = os.cpu_count() or 1
@@ -158,13 +195,15 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak" if (args.shard == "batch" and args.gpus > 1) else "strong",
         "vs_baseline": None, "dtype": "f32 (numpy)", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K},
+        "config": headline_config(args.gpus, args.shard),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nproc, "kind": "port",
                          "sample": f"{args.cpu_rows} rows of A and of W^T encoded per step "
                                    "(literal LUT search, process pool), full-tensor amax, "
-                                   f"{args.cpu_rows}-row dequant + sgemm; extrapolated by rows"},
+                                   f"{args.cpu_rows}-row dequant + sgemm; extrapolated by rows "
+                                   "to the whole single-GPU C2 step"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -177,6 +216,30 @@ def host_inputs_numpy():
     of the bf16 values), generated with the same seeded torch generator."""
     A, Wt = make_inputs("cpu")
     return A.float().numpy(), Wt.float().numpy()
+
+
+def _warm_pool(pool, nproc):
+    import numpy as np
+    list(pool.map(_cpu_encode_rows, [(np.zeros((1, 16), np.float32), 1.0, "E4M3")] * nproc))
+
+
+def cpu_baseline(args):
+    """Rank 0, N = 1: the oracle port of the reference, bounded sample."""
+    if args.cpu_rows is None:
+        args.cpu_rows = 64
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
+    A_np, Wt_np = host_inputs_numpy()
+    nproc = os.cpu_count() or 1
+    with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as pool:
+        _warm_pool(pool, nproc)
+        sec, parts = cpu_reference_step(A_np, Wt_np, args.cpu_rows, pool, nproc)
+    return {"value": FLOPS / sec / 1e12, "unit": "TFLOP/s", "cores": nproc, "kind": "port",
+            "sample": f"{args.cpu_rows} rows of A and of W^T encoded (literal LUT search, "
+                      f"{nproc} spawn processes), full-tensor amax, {args.cpu_rows}-row dequant "
+                      "+ sgemm; extrapolated linearly by rows",
+            "seconds_per_step": sec,
+            "breakdown_s": {k: round(v, 3) for k, v in parts.items()}}
 
 
 # --------------------------------------------------------------- GPU side
@@ -277,11 +340,136 @@ def measured_peaks():
             "fallback"
 
 
+
+
+# --------------------------------------------------------------- timing helpers
+
+
+def _dist():
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist, dist.get_world_size(), dist.get_rank()
+    return None, 1, 0
+
+
+def _barrier():
+    import torch
+    d, world, _ = _dist()
+    torch.cuda.synchronize()
+    if world > 1:
+        d.barrier(device_ids=[torch.cuda.current_device()])
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(values):
+    """Element-wise max of a list of floats over ranks (device collective)."""
+    import torch
+    d, world, _ = _dist()
+    if world == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device="cuda")
+    d.all_reduce(t, op=d.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _time_graph(fns, reps=None, warm=2):
+    """Device time (ms) per call of one of ``fns`` (a callable or a list of
+    callables, e.g. the same op over several rotating input buffers). The
+    calls are captured once in a CUDA graph and replayed ``reps`` times,
+    so short kernels are timed without the host's launch overhead; CUDA
+    events on the replaying stream, after warm-up replays."""
+    import torch
+    fns = list(fns) if isinstance(fns, (list, tuple)) else [fns]
+    if reps is None:
+        reps = max(2, math.ceil(12 / len(fns)))
+    for _ in range(warm):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for f in fns:
+                f()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(warm):
+        g.replay()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(fns))
+    del g
+    return ms
+
+
+def _rotation(nbytes):
+    """Copies of an input to rotate through so that the data a launch reads
+    (``nbytes`` per copy) was not left in L2 by the launches before it: the
+    copies together exceed three times the L2."""
+    return max(1, math.ceil(3 * L2_BYTES / max(nbytes, 1)))
+
+
+def _pick(n, k, seed):
+    """k indices in [0, n) with the first and last and tile edges."""
+    import numpy as np
+    g = np.random.default_rng(seed)
+    edges = [i for i in (0, 127, 128, 255, 256, n // 2, n - 129, n - 128, n - 1) if 0 <= i < n]
+    return np.unique(np.concatenate([edges, g.choice(n, size=min(k, n), replace=False)]))
+
+
+def _rel_cos(got, ref):
+    import numpy as np
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rel = float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+    cos = float((got.ravel() @ ref.ravel()) /
+                (np.linalg.norm(got) * np.linalg.norm(ref) + 1e-300))
+    return rel, cos
+
+
+# --------------------------------------------------------------- headline
+
+
+def headline_parity(A, Wt_sh, out, recipe):
+    """This rank's C[:, n0:n1] on 64 sampled rows x 256 sampled columns
+    against the CPU oracle: the reference's casts of those rows (with the
+    amax of the whole A and of the whole weight over all ranks' shards, as
+    cast.py:364-373 takes it) and its dequantize-then-float32 matmul. Run
+    once, outside the timed region. Max over ranks of the relative error,
+    min of the cosine."""
+    import numpy as np
+    import torch
+    from oracle import cast as ocast, codec
+    A_h = A.cpu()
+    W_h = Wt_sh.cpu()
+    amax_a = codec.tensor_amax(A_h.abs().max().float().numpy())
+    w_local = float(W_h.abs().max().float()) if W_h.numel() else 0.0
+    amax_w = codec.tensor_amax(np.float64(_max_over_ranks([w_local])[0]))
+    rows, cols = _pick(A_h.shape[0], 64, 5), _pick(W_h.shape[0], 256, 6)
+    qa = ocast.cast_per_tensor_fp8(A_h[rows].float().numpy(), recipe, amax=amax_a)
+    qw = ocast.cast_per_tensor_fp8(W_h[cols].float().numpy(), recipe, amax=amax_w)
+    ref = ocast.matmul(qa, ocast.dequantize(qw).T)
+    got = out[torch.as_tensor(rows, device=out.device)][:, torch.as_tensor(cols, device=out.device)]
+    rel, cos = _rel_cos(got.float().cpu().numpy(), ref)
+    rel, ncos = _max_over_ranks([rel, -cos])
+    return {"rows": int(len(rows)), "cols_per_rank": int(len(cols)), "max_rel": rel,
+            "cos": -ncos, "ok": bool(rel <= 1e-2 and -ncos >= 0.9999),
+            "tolerance": "max|gpu-ref|/max|ref| <= 1e-2 and cosine >= 0.9999 against the "
+                         "oracle's float32 matmul of the same casts (bf16 output)"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
     import breccia_b200 as bb
-    from breccia_b200.dist import shard_rows, cast_per_tensor_sharded, cast_per_tensor_async
+    from breccia_b200.dist import shard_rows, cast_per_tensor_async, cast_weight_split
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -293,17 +481,13 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     recipe = bb.Float8CurrentScaling(fp8_format="E4M3")
-    batch = args.shard == "batch"
+    batch = args.shard == "batch" and world > 1
     A, Wt = make_inputs(dev, batch_seed=(1000 + rank) if batch and rank > 0 else None)
-    n0, n1 = (0, N) if batch else shard_rows(N, world, rank)
+    n0, n1 = (0, N) if (batch or world == 1) else shard_rows(N, world, rank)
     Wt_sh = Wt[n0:n1].contiguous()
     del Wt
     torch.cuda.synchronize()
     job_flops = FLOPS * (world if batch else 1)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
 
     gemm_events = []
 
@@ -315,8 +499,7 @@ def run_ours(args):
             sw = bb.cast(w_in, recipe)
             sa = pending.wait()
         else:
-            sa = bb.cast(a_in, recipe)
-            sw = cast_per_tensor_sharded(w_in, recipe)
+            sa, sw = cast_weight_split(a_in, w_in, recipe)
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
@@ -329,28 +512,28 @@ def run_ours(args):
 
     # ---- device-resident timing
     for _ in range(args.warmup):
-        step(A, Wt_sh)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid) \
-        if hasattr(torch.cuda.get_device_properties(dev), "uuid") else None
+        out = step(A, Wt_sh)
+    _barrier()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else None
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with Clocks(uuid) as clk:
         t_start.record()
         for _ in range(args.steps):
-            step(A, Wt_sh, record=True)
+            out = step(A, Wt_sh, record=True)
         t_end.record()
         torch.cuda.synchronize()
-    barrier()
+    _barrier()
     ms = t_start.elapsed_time(t_end) / args.steps
     gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
-    ms_t = torch.tensor([ms, gemm_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms, gemm_ms_max = ms_t.tolist()
+    ms, gemm_ms_max = _max_over_ranks([ms, gemm_ms])
     value = job_flops / (ms * 1e-3) / 1e12
+
+    parity = None
+    if not args.no_parity:
+        parity = headline_parity(A, Wt_sh, out, recipe) if not batch else None
+    del out
 
     # ---- end to end through the public API, host buffers
     # Every step copies its own inputs from pinned host memory and its result
@@ -393,8 +576,7 @@ def run_ours(args):
                     ev_down[b].record(s_d2h)
 
         e2e_steps(max(2, args.warmup))
-        torch.cuda.synchronize()
-        barrier()
+        _barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(s_h2d)
@@ -405,40 +587,53 @@ def run_ours(args):
         s_h2d.wait_stream(s_cmp)
         e1.record(s_h2d)
         torch.cuda.synchronize()
-        barrier()
-        e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+        _barrier()
+        e_ms = _max_over_ranks([e0.elapsed_time(e1) / args.steps])[0]
+        h2d = A_h.numel() * 2 + W_h.numel() * 2
+        d2h = out_h[0].numel() * 2
         if world > 1:
-            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": job_flops / (e_ms.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": A_h.numel() * 2 + W_h.numel() * 2,
-               "d2h_bytes_per_step": out_h[0].numel() * 2,
-               "ms_per_step": e_ms.item(),
+            hb = torch.tensor([h2d, d2h], device=dev, dtype=torch.float64)
+            dist.all_reduce(hb)
+            h2d, d2h = [int(v) for v in hb.tolist()]
+        e2e = {"value": job_flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
                "pipelining": "uploads, kernels and downloads of consecutive steps overlap "
                              "(3 streams, 2 buffers)"}
-        if world > 1:
-            hb = torch.tensor([e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]],
-                              device=dev, dtype=torch.float64)
-            dist.all_reduce(hb)
-            e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"] = [int(v) for v in hb.tolist()]
+        del A_h, W_h, out_h, A_d, W_d, outs
 
-    # ---- roofline of the dominant kernel (the GEMM), per rank
+    # ---- roofline of the dominant kernel (the GEMM), this rank's shard
     peaks, src = measured_peaks()
-    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    peak_fp8 = 2.0 * peaks["bf16_tflops"]
     gemm_flops_rank = 2.0 * M * (n1 - n0) * K
-    achieved = gemm_flops_rank / (gemm_ms * 1e-3) / 1e12
+    achieved = gemm_flops_rank / (gemm_ms_max * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_fp8, "unit": "TFLOP/s",
-                "frac": achieved / peak_fp8, "traffic": GEMM_DRAM_BYTES,
+                "frac": achieved / peak_fp8,
+                "traffic": GEMM_DRAM_BYTES if (world == 1 or batch) else None,
+                "traffic_source": "one ncu capture of this GEMM at this shape on one B200 "
+                                  "(dram__bytes_read.sum + dram__bytes_write.sum), not measured "
+                                  "in this run" if (world == 1 or batch) else None,
+                "algorithmic_bytes": (M * K + (n1 - n0) * K + 2 * M * (n1 - n0)),
                 "kernel": "brc::gemm::k_gemm_pair<kPerTensor,E4M3,E4M3,bf16>",
-                "peak_source": f"2 x bf16_tflops_sustained of {src} MEASURED_PEAKS.json "
-                               "(dense FP8 = 2x dense bf16)",
-                "frac_vs_burst": achieved / (2.0 * peaks["bf16_tflops"]),
-                "gemm_ms": gemm_ms}
+                "peak_source": f"dense FP8 = 2 x bf16_tflops (burst, {src} MEASURED_PEAKS.json; "
+                               "the timed region is well under a second)",
+                "frac_vs_sustained": achieved / (2.0 * peaks["bf16_tflops_sustained"]),
+                "gemm_ms": gemm_ms_max, "gemm_share_of_step": gemm_ms_max / ms}
+    del A, Wt_sh
+    torch.cuda.empty_cache()
 
-    extras = {}
-    if args.per_recipe and world == 1:
-        del A, Wt_sh
+    sharded = None
+    if not args.no_sharded and not batch:
+        sharded = sharded_configs(peaks, args)
         torch.cuda.empty_cache()
+
+    extras, libref = {}, None
+    if world == 1 and not args.no_per_recipe:
         extras = per_recipe(peaks, src)
+        torch.cuda.empty_cache()
+        libref = library_reference(peaks)
+        if libref and libref.get("c2_pertensor_fp8", {}).get("TFLOP/s"):
+            roofline["frac_vs_cublaslt_same_shape"] = \
+                achieved / libref["c2_pertensor_fp8"]["TFLOP/s"]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -455,116 +650,185 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "e4m3 x e4m3 -> f32 accumulate -> bf16 out",
             "data": "synthetic (seeded torch generator, BASELINE configs[1] shapes/distributions)",
-            "config": {"workload": WORKLOAD, "M": M * (world if batch else 1), "N": N, "K": K,
-                       "M_per_gpu": M,
-                       "parallelism": "single GPU" if world == 1 else
-                       (f"data parallel over {world} GPUs: {M} activation rows per GPU, W "
-                        "replicated, one NCCL all-reduce(MAX) of the activations' amax "
-                        "(overlapped with the weight cast)") if batch else
-                       f"W^T split along N over {world} GPUs, A replicated, "
-                       "one NCCL all-reduce(MAX) of the weight amax",
-                       "l2": "inputs larger than L2 (A is 268 MB)"},
+            "config": headline_config(world, args.shard),
             "clocks": clk.summary(),
             "e2e": e2e,
             "gpu_launches": 7 * args.steps * world,
-            "gpu_launches_per_rank": 7 * args.steps,
+            "gpu_launches_per_rank_per_step": {"amax_reset": 2, "amax": 2, "encode": 2, "gemm": 1},
+            "parity": parity,
             "roofline": roofline,
             "cpu_baseline": cpu,
         }
+        if sharded:
+            line["sharded"] = sharded
         if extras:
             line["per_recipe"] = extras
+        if libref:
+            line["library_reference"] = libref
         print(json.dumps(line), flush=True)
     return 0
 
 
-def _warm_pool(pool, nproc):
-    import numpy as np
-    list(pool.map(_cpu_encode_rows, [(np.zeros((1, 16), np.float32), 1.0, "E4M3")] * nproc))
+# --------------------------------------------------------------- sharded configs
 
 
-def cpu_baseline(args):
-    """Rank 0, N = 1: the oracle port of the reference, bounded sample."""
-    if args.cpu_rows is None:
-        args.cpu_rows = 64
-    import multiprocessing as mp
-    from concurrent.futures import ProcessPoolExecutor
-    A_np, Wt_np = host_inputs_numpy()
-    nproc = os.cpu_count() or 1
-    with ProcessPoolExecutor(max_workers=nproc, mp_context=mp.get_context("spawn")) as pool:
-        _warm_pool(pool, nproc)
-        sec, parts = cpu_reference_step(A_np, Wt_np, args.cpu_rows, pool, nproc)
-    return {"value": FLOPS / sec / 1e12, "unit": "TFLOP/s", "cores": nproc, "kind": "port",
-            "sample": f"{args.cpu_rows} rows of A and of W^T encoded (literal LUT search, "
-                      f"{nproc} spawn processes), full-tensor amax, {args.cpu_rows}-row dequant "
-                      "+ sgemm; extrapolated linearly by rows",
-            "seconds_per_step": sec,
-            "breakdown_s": {k: round(v, 3) for k, v in parts.items()}}
+def sharded_configs(peaks, args):
+    """BASELINE configs 2-5 with the weight split along N over the ranks
+    (W^T rows [n0, n1) per rank, ``shard_rows``), activations replicated.
+    Every figure is timed on every rank (CUDA-graph replay of the rank's own
+    kernels; no collective inside) and reported for the whole job: the full
+    GEMM's FLOPs, or the full weight's bytes, over the slowest rank's time.
+    The replicated activation casts do not shrink with N and are reported
+    apart. One rank gives the unsharded baseline of the same figures.
+    Operands are rotated so each launch reads data not left in L2."""
+    import torch
+    import breccia_b200 as bb
+    from breccia_b200.dist import shard_rows
+    _, world, rank = _dist()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm = peaks["hbm_gbs"]
+    fp8, fp4 = 2.0 * peaks["bf16_tflops"], 4.0 * peaks["bf16_tflops"]
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    res = {"n_ranks": world,
+           "layout": "W^T rows split over the ranks (128-aligned), activations replicated; "
+                     "job figures = whole GEMM FLOPs or whole weight bytes / max rank time"}
+
+    def timed(fns):
+        _barrier()
+        return _max_over_ranks([_time_graph(fns)])[0]
+
+    def block_config(tag, Mc, Nc, Kc, r, heavy, peak, a_bytes_el, w_bytes_el):
+        lo, hi = shard_rows(Nc, world, rank)
+        A = torch.randn(Mc, Kc, generator=g, device=dev).to(torch.bfloat16)
+        if heavy:
+            t = torch.distributions.StudentT(torch.tensor(4.0, device=dev))
+            Wsh = (t.sample((hi - lo, Kc)) * 0.02).to(torch.bfloat16)
+        else:
+            Wsh = (torch.randn(hi - lo, Kc, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        ra = _rotation(A.numel() * a_bytes_el)
+        As = [A] + [A.clone() for _ in range(ra - 1)]
+        ms_a = timed([lambda x=x: bb.cast(x, r) for x in As])
+        rw = _rotation(Wsh.numel() * w_bytes_el)
+        Ws = [Wsh] + [Wsh.clone() for _ in range(rw - 1)]
+        ms_w = timed([lambda x=x: bb.cast(x, r) for x in Ws])
+        del As, Ws
+        sa0, sw0 = bb.cast(A, r), bb.cast(Wsh, r)
+        op_bytes = sa0.data.numel() + sw0.data.numel()
+        if r.name == "nvfp4":
+            op_bytes //= 2
+        rg = _rotation(op_bytes)
+        pairs = [(sa0, sw0)] + [(bb.cast(A, r), bb.cast(Wsh, r)) for _ in range(rg - 1)]
+        ms_g = timed([lambda p=p: bb.linear(p[0], p[1], out_dtype=torch.bfloat16)
+                      for p in pairs])
+        del pairs, sa0, sw0, A, Wsh
+        torch.cuda.empty_cache()
+        flops = 2.0 * Mc * Nc * Kc
+        wbytes = Nc * Kc * w_bytes_el
+        res[tag] = {
+            "gemm_ms_max_rank": ms_g, "gemm_job_TFLOP/s": flops / (ms_g * 1e-3) / 1e12,
+            "gemm_frac_per_gpu": flops / world / (ms_g * 1e-3) / 1e12 / peak,
+            "cast_W_ms_max_rank": ms_w, "cast_W_job_GB/s": wbytes / (ms_w * 1e-3) / 1e9,
+            "cast_W_frac_per_gpu": wbytes / world / (ms_w * 1e-3) / 1e9 / hbm,
+            "cast_A_replicated_ms": ms_a,
+            "cast_A_GB/s": Mc * Kc * a_bytes_el / (ms_a * 1e-3) / 1e9,
+            "rows_per_rank": hi - lo, "rotated_copies": {"A": ra, "W": rw, "gemm": rg}}
+
+    # C3 MXFP8: A bf16 (8192, 8192), W^T bf16 (28672, 8192); bytes per element:
+    # 2 in + 1 code + 1/32 scale + 1/32 scale atom
+    block_config("c3_mxfp8", 8192, 28672, 8192, bb.MXFP8BlockScaling(), False, fp8,
+                 2 + 1 + 2 / 32, 2 + 1 + 2 / 32)
+    # C4 NVFP4: A bf16 (4096, 8192), W^T Student-t(4) * 0.02; 2 in + 1 code +
+    # 0.5 packed + 2/16 (scale + atom)
+    block_config("c4_nvfp4", 4096, 28672, 8192, bb.NVFP4BlockScaling(), True, fp4,
+                 2 + 1.5 + 2 / 16, 2 + 1.5 + 2 / 16)
+
+    # C5 INT4 asymmetric g128: W^T f32 (28672, 8192) shard; GEMV of M = 1, 4, 16
+    # bf16 activation rows against it (dequantization fused, weight read once)
+    Nc, Kc = 28672, 8192
+    lo, hi = shard_rows(Nc, world, rank)
+    r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
+    Wsh = torch.randn(hi - lo, Kc, generator=g, device=dev) * 0.02
+    # f32 in, 1 code byte, 0.5 tile byte, per group: f16 scale + zp, f32 scale + zp tiles
+    cast_b = 4 + 1 + 0.5 + 12 / 128
+    rw = _rotation(Wsh.numel() * cast_b)
+    Ws = [Wsh] + [Wsh.clone() for _ in range(rw - 1)]
+    ms_w = timed([lambda x=x: bb.cast(x, r) for x in Ws])
+    del Ws
+    gemv_w = 0.5 + 8 / 128  # packed codes + f32 scale and zp tiles per element
+    rg = _rotation(Wsh.numel() * gemv_w)
+    sws = [bb.cast(Wsh, r) for _ in range(rg)]
+    del Wsh
+    c5 = {"cast_W_ms_max_rank": ms_w,
+          "cast_W_job_GB/s": Nc * Kc * cast_b / (ms_w * 1e-3) / 1e9,
+          "cast_W_frac_per_gpu": Nc * Kc * cast_b / world / (ms_w * 1e-3) / 1e9 / hbm,
+          "rows_per_rank": hi - lo, "rotated_copies": {"W": rw, "gemv": rg}}
+    for m in (1, 4, 16):
+        A = torch.randn(m, Kc, generator=g, device=dev).to(torch.bfloat16)
+        ms = timed([lambda sw=sw: bb.linear(A, sw, out_dtype=torch.bfloat16) for sw in sws])
+        b = Nc * Kc * gemv_w + m * Kc * 2 * world + m * Nc * 2
+        c5[f"gemv_M{m}_ms_max_rank"] = ms
+        c5[f"gemv_M{m}_job_GB/s"] = b / (ms * 1e-3) / 1e9
+        c5[f"gemv_M{m}_frac_per_gpu"] = b / world / (ms * 1e-3) / 1e9 / hbm
+    res["c5_int4_gemv"] = c5
+    del sws
+    torch.cuda.empty_cache()
+    return res
 
 
 # --------------------------------------------------------------- per recipe
 
 
-def _time_ms(fn, iters=10, warm=3, graph=True):
-    """Device time per call. With graph=True the call is captured once in a
-    CUDA graph and replayed, so small kernels are timed without the Python
-    launch overhead of the wrapper (the GPU would otherwise idle between
-    launches); each replay runs the same kernels with the same arguments."""
-    import torch
-    for _ in range(warm):
-        fn()
-    torch.cuda.synchronize()
-    run = fn
-    if graph:
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                fn()
-        torch.cuda.current_stream().wait_stream(s)
-        run = g.replay
-        run()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(iters):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / iters
-
-
 def per_recipe(peaks, src):
-    """Every BASELINE config at full size on one GPU: cast GB/s (algorithmic
-    bytes: input read once -- twice for per-tensor, whose global amax must be
-    known before any code is written -- plus codes, scales and side outputs
-    written) and GEMM TFLOP/s. Inputs exceed L2 except where noted."""
+    """Every BASELINE config at full size on one GPU. Casts, dequantize and
+    requantize in GB/s of algorithmic bytes (input read once -- twice for
+    per-tensor, whose global amax must be known before any code is written
+    -- plus codes, scales and side outputs written); GEMMs in TFLOP/s; each
+    with its fraction of the measured burst peaks (HBM copy; dense FP8 /
+    FP4 = 2x / 4x dense bf16). Inputs smaller than three L2s are rotated
+    over copies, so every figure is an HBM figure."""
     import torch
     import breccia_b200 as bb
+    from breccia_b200 import _lib as L
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(1)
     hbm = peaks["hbm_gbs"]
-    fp8 = 2.0 * peaks["bf16_tflops_sustained"]
-    fp4 = 4.0 * peaks["bf16_tflops_sustained"]
+    fp8 = 2.0 * peaks["bf16_tflops"]
+    fp4 = 4.0 * peaks["bf16_tflops"]
     res = {}
 
-    def cast_entry(name, x, r, bytes_, **kw):
-        ms = _time_ms(lambda: bb.cast(x, r, **kw))
+    def copies(x, nbytes):
+        return [x] + [x.clone() for _ in range(_rotation(nbytes) - 1)]
+
+    def bw_entry(name, fns, bytes_, **extra):
+        ms = _time_graph(fns)
         gbs = bytes_ / (ms * 1e-3) / 1e9
-        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm}
+        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
+                     "rotated_copies": len(fns) if isinstance(fns, list) else 1, **extra}
+
+    def cast_entry(name, x, r, bytes_, **kw):
+        xs = copies(x, bytes_)
+        bw_entry(name, [lambda xi=xi: bb.cast(xi, r, **kw) for xi in xs], bytes_)
+        del xs
+
+    def dequant_entry(name, st, bytes_):
+        sts = [st] + [_clone_st(st) for _ in range(_rotation(bytes_) - 1)]
+        bw_entry(name, [lambda s=s: bb.dequantize(s) for s in sts], bytes_)
+        del sts
 
     def ste_entry(name, x, r, bytes_):
         # fused cast_ste forward vs the unfused cast -> dequantize -> x + (y - x)
-        ms = _time_ms(lambda: bb.cast_ste(x, r))
-        ms_u = _time_ms(lambda: x + (bb.dequantize(bb.cast(x, r)) - x))
-        gbs = bytes_ / (ms * 1e-3) / 1e9
-        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm, "unfused_ms": ms_u}
+        xs = copies(x, bytes_)
+        ms_u = _time_graph([lambda xi=xi: xi + (bb.dequantize(bb.cast(xi, r)) - xi) for xi in xs])
+        bw_entry(name, [lambda xi=xi: bb.cast_ste(xi, r) for xi in xs], bytes_, unfused_ms=ms_u)
+        del xs
 
-    def gemm_entry(name, a, w, m, n, k, peak):
-        ms = _time_ms(lambda: bb.linear(a, w, out_dtype=torch.bfloat16))
+    def gemm_entry(name, make_pair, m, n, k, peak, op_bytes, out_dtype=torch.bfloat16):
+        pairs = [make_pair() for _ in range(_rotation(op_bytes))]
+        ms = _time_graph([lambda p=p: bb.linear(p[0], p[1], out_dtype=out_dtype) for p in pairs])
         tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
-        res[name] = {"ms": ms, "TFLOP/s": tf, "frac_peak": tf / peak}
+        res[name] = {"ms": ms, "TFLOP/s": tf, "frac_peak": tf / peak,
+                     "rotated_copies": len(pairs)}
+        del pairs
 
     # C1 Float8BlockScaling: A f32 (2048, 7168) 1x128; W^T f32 (4096, 7168) 128x128
     A = torch.randn(2048, 7168, generator=g, device=dev)
@@ -573,18 +837,29 @@ def per_recipe(peaks, src):
     cast_entry("c1_cast_A_block1x128_f32", A, r, A.numel() * 5 + A.numel() // 128 * 4)
     cast_entry("c1_cast_Wt_block128x128_f32", Wt, r, Wt.numel() * 5 + Wt.numel() // 16384 * 4,
                block_m=128)
-    ms = _time_ms(lambda: bb.linear(bb.cast(A, r), bb.cast(Wt, r, block_m=128),
-                                    out_dtype=torch.float32))
+    sa = bb.cast(A, r)
+    dequant_entry("c1_dequant_A_block1x128_to_f32", sa, A.numel() * 5 + A.numel() // 128 * 4)
+    gemm_entry("c1_gemm_block_fp8_f32out", lambda: (bb.cast(A, r), bb.cast(Wt, r, block_m=128)),
+               2048, 4096, 7168, fp8, (A.numel() + Wt.numel()), out_dtype=torch.float32)
+    As, Ws = copies(A, A.numel() * 5), copies(Wt, Wt.numel() * 5)
+    ms = _time_graph([lambda a=a, w=w: bb.linear(bb.cast(a, r), bb.cast(w, r, block_m=128),
+                                                 out_dtype=torch.float32)
+                      for a, w in zip(As, Ws)])
     res["c1_step_cast_both_gemm_block_fp8_f32out"] = {
-        "ms": ms, "TFLOP/s": 2.0 * 2048 * 4096 * 7168 / (ms * 1e-3) / 1e12}
-    gemm_entry("c1_gemm_block_fp8", bb.cast(A, r), bb.cast(Wt, r, block_m=128), 2048, 4096, 7168,
-               fp8)
-    del A, Wt
-    # C2 per-tensor: A bf16 (16384, 8192): two reads + one write
+        "ms": ms, "TFLOP/s": 2.0 * 2048 * 4096 * 7168 / (ms * 1e-3) / 1e12,
+        "rotated_copies": len(As)}
+    del A, Wt, sa, As, Ws
+
+    # C2 per-tensor: A bf16 (16384, 8192) -- two reads + one write; W^T bf16 (8192, 8192)
     A = torch.randn(16384, 8192, generator=g, device=dev).to(torch.bfloat16)
-    cast_entry("c2_cast_A_pertensor_bf16", A, bb.Float8CurrentScaling(), A.numel() * 5)
-    ste_entry("c2_cast_ste_A_pertensor_bf16", A, bb.Float8CurrentScaling(), A.numel() * 8)
-    del A
+    rc = bb.Float8CurrentScaling()
+    cast_entry("c2_cast_A_pertensor_bf16", A, rc, A.numel() * 5)
+    Wt = (torch.randn(8192, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    cast_entry("c2_cast_Wt_pertensor_bf16", Wt, rc, Wt.numel() * 5)
+    dequant_entry("c2_dequant_A_pertensor_to_f32", bb.cast(A, rc), A.numel() * 5)
+    ste_entry("c2_cast_ste_A_pertensor_bf16", A, rc, A.numel() * 8)
+    del A, Wt
+
     # C3 MXFP8: A bf16 (8192, 8192), W^T bf16 (28672, 8192); GEMM 8192 x 28672 x 8192
     r = bb.MXFP8BlockScaling()
     A = torch.randn(8192, 8192, generator=g, device=dev).to(torch.bfloat16)
@@ -592,8 +867,14 @@ def per_recipe(peaks, src):
     cast_entry("c3_cast_A_mxfp8_bf16", A, r, A.numel() * 3 + A.numel() // 32 * 2)
     cast_entry("c3_cast_Wt_mxfp8_bf16", Wt, r, Wt.numel() * 3 + Wt.numel() // 32 * 2)
     ste_entry("c3_cast_ste_A_mxfp8_bf16", A, r, A.numel() * 6)
-    gemm_entry("c3_gemm_mxfp8", bb.cast(A, r), bb.cast(Wt, r), 8192, 28672, 8192, fp8)
-    del A, Wt
+    sw = bb.cast(Wt, r)
+    dequant_entry("c3_dequant_Wt_mxfp8_to_f32", sw, Wt.numel() * 5 + Wt.numel() // 32)
+    del sw
+    sa = bb.cast(A, r)
+    gemm_entry("c3_gemm_mxfp8", lambda: (sa, bb.cast(Wt, r)), 8192, 28672, 8192, fp8,
+               A.numel() + Wt.numel())
+    del A, Wt, sa
+
     # C4 NVFP4: A bf16 (4096, 8192), W^T bf16 (28672, 8192) Student-t(4) * 0.02
     r = bb.NVFP4BlockScaling()
     A = torch.randn(4096, 8192, generator=g, device=dev).to(torch.bfloat16)
@@ -602,18 +883,19 @@ def per_recipe(peaks, src):
     cast_entry("c4_cast_A_nvfp4_bf16", A, r, A.numel() * 3.5 + A.numel() // 16 * 2)
     cast_entry("c4_cast_Wt_nvfp4_bf16", Wt, r, Wt.numel() * 3.5 + Wt.numel() // 16 * 2)
     sw = bb.cast(Wt, r)
-    gemm_entry("c4_gemm_nvfp4", bb.cast(A, r), sw, 4096, 28672, 8192, fp4)
-    ms = _time_ms(lambda: bb.requantize(sw, bb.MXFP8BlockScaling()))
+    dequant_entry("c4_dequant_Wt_nvfp4_to_f32", sw, Wt.numel() * 5 + Wt.numel() // 16)
+    sa = bb.cast(A, r)
+    gemm_entry("c4_gemm_nvfp4", lambda: (sa, bb.cast(Wt, r)), 4096, 28672, 8192, fp4,
+               (A.numel() + Wt.numel()) // 2)
     n = Wt.numel()
     b = n * 1 + n // 16 + n * 1 + n // 32 * 2
-    res["c4_requant_Wt_nvfp4_to_mxfp8"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
-                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
+    bw_entry("c4_requant_Wt_nvfp4_to_mxfp8", lambda: bb.requantize(sw, bb.MXFP8BlockScaling()),
+             b)
     # loading the C4 weight from breccia's packed on-disk order (bridges): unpack to
     # codes + tensor-core packed order, and rebuild the scale atoms
-    from breccia_b200 import _lib as L
-    st_ = torch.cuda.current_stream().cuda_stream
     pk = torch.empty(n // 2, dtype=torch.uint8, device=dev)
-    L.call("brc_pack_nibbles_hi", sw.data.data_ptr(), n, pk.data_ptr(), st_)
+    L.call("brc_pack_nibbles_hi", sw.data.data_ptr(), n, pk.data_ptr(),
+           torch.cuda.current_stream().cuda_stream)
     codes_ = torch.empty(n, dtype=torch.uint8, device=dev)
     lo_ = torch.empty(n // 2, dtype=torch.uint8, device=dev)
     atoms_ = torch.empty(bb.gemm_operands(sw)["sf_mma"].numel(), dtype=torch.uint8, device=dev)
@@ -622,44 +904,149 @@ def per_recipe(peaks, src):
         s_ = torch.cuda.current_stream().cuda_stream  # the capturing stream under a graph
         L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes_.data_ptr(), lo_.data_ptr(), s_)
         L.call("brc_scale_atoms", sw.scale.data_ptr(), 28672, 8192 // 16, atoms_.data_ptr(), s_)
-    ms = _time_ms(_load_nvfp4)
-    b = n // 2 + n // 16 + n + n // 2 + atoms_.numel()
-    res["c4_load_Wt_nvfp4_from_packed"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
-                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
-    del A, Wt, sw, pk, codes_, lo_, atoms_
+    bw_entry("c4_load_Wt_nvfp4_from_packed", _load_nvfp4,
+             n // 2 + n // 16 + n + n // 2 + atoms_.numel())
+    del A, Wt, sw, sa, pk, codes_, lo_, atoms_
+    torch.cuda.empty_cache()
+
     # C5 INT4 asymmetric g128: W^T f32 (28672, 8192)
     Wt = torch.randn(28672, 8192, generator=g, device=dev) * 0.02
     r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
-    cast_entry("c5_cast_Wt_int4_asym_f32", Wt, r,
-               Wt.numel() * 5.5 + Wt.numel() // 128 * 4)
+    cast_entry("c5_cast_Wt_int4_asym_f32", Wt, r, Wt.numel() * 5.5 + Wt.numel() // 128 * 12)
     sw = bb.cast(Wt, r)
-    del Wt
+    n = sw.data.numel()
+    dequant_entry("c5_dequant_Wt_int4_asym_to_f32", sw, n * 5 + n // 128 * 4)
     # rebuilding the skinny-GEMM tiles of a stored (loaded) C5 weight
     tl = bb.gemm_operands(sw)
-    n = sw.data.numel()
 
     def _tiles():
         L.call("brc_int4_tiles", sw.data.data_ptr(), 28672, 8192, sw.scale.data_ptr(),
                sw.zero_point.data_ptr(), L.SCALE_F16, tl["int4_tiles"].data_ptr(),
                tl["int4_scale_tiles"].data_ptr(), tl["int4_zp_tiles"].data_ptr(),
                torch.cuda.current_stream().cuda_stream)
-    ms = _time_ms(_tiles)
-    b = n + n // 128 * 2 * 2 + n // 2 + n // 128 * 4 * 2
-    res["c5_int4_tiles_from_stored_Wt"] = {"ms": ms, "GB/s": b / (ms * 1e-3) / 1e9,
-                                           "frac_hbm": b / (ms * 1e-3) / 1e9 / hbm}
+    bw_entry("c5_int4_tiles_from_stored_Wt", _tiles,
+             n + n // 128 * 2 * 2 + n // 2 + n // 128 * 4 * 2)
+    del sw, tl
+    gemv_b = n // 2 + n // 128 * 8
+    sws = [bb.cast(Wt, r) for _ in range(_rotation(gemv_b))]
+    del Wt
     for m in (1, 4, 16):
         A = torch.randn(m, 8192, generator=g, device=dev).to(torch.bfloat16)
-        ms = _time_ms(lambda: bb.linear(A, sw, out_dtype=torch.bfloat16), iters=50)
-        b = 28672 * 8192 // 2 + 2 * (28672 * 64 * 2) + m * 8192 * 2 + m * 28672 * 2
+        ms = _time_graph([lambda sw=sw: bb.linear(A, sw, out_dtype=torch.bfloat16)
+                          for sw in sws], reps=8)
+        b = gemv_b + m * 8192 * 2 + m * 28672 * 2
         gbs = b / (ms * 1e-3) / 1e9
         res[f"c5_gemv_int4_M{m}"] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
-                                     "TFLOP/s": 2.0 * m * 28672 * 8192 / (ms * 1e-3) / 1e12}
-    del sw
+                                     "TFLOP/s": 2.0 * m * 28672 * 8192 / (ms * 1e-3) / 1e12,
+                                     "rotated_copies": len(sws)}
+    del sws
     torch.cuda.empty_cache()
     res["peaks"] = {"hbm_gbs": hbm, "fp8_tflops": fp8, "fp4_tflops": fp4,
-                    "source": f"{src} MEASURED_PEAKS.json: hbm_gbs; 2x / 4x "
-                              "bf16_tflops_sustained for dense FP8 / FP4"}
+                    "source": f"{src} MEASURED_PEAKS.json: hbm_gbs (copy); 2x / 4x bf16_tflops "
+                              "(burst) for dense FP8 / FP4 (hardware ratios; cuBLASLt's own "
+                              "FP8 / FP4 GEMMs on this box are in library_reference)"}
     return res
+
+
+def _clone_st(st):
+    """An independent copy of a ScaledTensor (same recipe and layout)."""
+    zp = getattr(st, "zero_point", None)
+    return type(st)(data=st.data.clone(), scale=st.scale.clone(), recipe=st.recipe,
+                    layout=st.layout, zero_point=None if zp is None else zp.clone())
+
+
+# --------------------------------------------------------------- library reference
+
+
+def library_reference(peaks):
+    """cuBLASLt's scaled GEMMs (torch.nn.functional.scaled_mm) on the operands
+    our casts produce, at the configs' shapes: a same-box reference point for
+    the dense FP8 / FP4 tensor-core rate, outside the product path. Each
+    result is checked against our GEMM's output (cosine) before its time is
+    reported; a variant torch refuses is reported as unavailable."""
+    import torch
+    import torch.nn.functional as F
+    import breccia_b200 as bb
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(2)
+    out = {}
+
+    def run(tag, m, n, k, ours_fn, lib_fn):
+        try:
+            ref = ours_fn().float()
+            got = lib_fn().float()
+            cos = float(torch.nn.functional.cosine_similarity(ref.flatten(), got.flatten(), 0))
+            if not cos >= 0.9999:
+                out[tag] = {"unavailable": f"result differs from ours (cosine {cos:.6f})"}
+                return
+            ms = _time_graph(lib_fn, reps=10)
+            ms_ours = _time_graph(ours_fn, reps=10)
+            out[tag] = {"ms": ms, "TFLOP/s": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
+                        "ours_ms_same_operands": ms_ours, "cosine_vs_ours": cos}
+        except Exception as e:  # a variant this torch / cuBLASLt does not offer
+            out[tag] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+        torch.cuda.empty_cache()
+
+    # C2 per-tensor FP8 (TensorWise)
+    r = bb.Float8CurrentScaling()
+    sa = bb.cast(torch.randn(16384, 8192, generator=g, device=dev).to(torch.bfloat16), r)
+    sw = bb.cast((torch.randn(8192, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16), r)
+    run("c2_pertensor_fp8", 16384, 8192, 8192,
+        lambda: bb.linear(sa, sw, out_dtype=torch.bfloat16),
+        lambda: F.scaled_mm(sa.data, sw.data.t(), sa.scale, F.ScalingType.TensorWise,
+                            sw.scale, F.ScalingType.TensorWise, output_dtype=torch.bfloat16))
+    del sa, sw
+
+    # C3 MXFP8 (1 x 32 E8M0 scales in the swizzled 32-4-4 layout our casts write)
+    r = bb.MXFP8BlockScaling()
+    sa = bb.cast(torch.randn(8192, 8192, generator=g, device=dev).to(torch.bfloat16), r)
+    sw = bb.cast((torch.randn(28672, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16), r)
+    oa, ow = bb.gemm_operands(sa), bb.gemm_operands(sw)
+    run("c3_mxfp8", 8192, 28672, 8192,
+        lambda: bb.linear(sa, sw, out_dtype=torch.bfloat16),
+        lambda: F.scaled_mm(sa.data.view(torch.float8_e4m3fn),
+                            sw.data.view(torch.float8_e4m3fn).t(),
+                            oa["sf_mma"].view(torch.float8_e8m0fnu),
+                            F.ScalingType.BlockWise1x32,
+                            ow["sf_mma"].view(torch.float8_e8m0fnu),
+                            F.ScalingType.BlockWise1x32,
+                            swizzle_a=F.SwizzleType.SWIZZLE_32_4_4,
+                            swizzle_b=F.SwizzleType.SWIZZLE_32_4_4,
+                            output_dtype=torch.bfloat16))
+    del sa, sw, oa, ow
+
+    # C4 NVFP4 (1 x 16 E4M3 scales, swizzled; packed E2M1 with element 2i in the low nibble)
+    r = bb.NVFP4BlockScaling()
+    sa = bb.cast(torch.randn(4096, 8192, generator=g, device=dev).to(torch.bfloat16), r)
+    sw = bb.cast((torch.randn(28672, 8192, generator=g, device=dev) * 0.02).to(torch.bfloat16), r)
+    oa, ow = bb.gemm_operands(sa), bb.gemm_operands(sw)
+    run("c4_nvfp4", 4096, 28672, 8192,
+        lambda: bb.linear(sa, sw, out_dtype=torch.bfloat16),
+        lambda: F.scaled_mm(oa["packed"].view(torch.float4_e2m1fn_x2),
+                            ow["packed"].view(torch.float4_e2m1fn_x2).t(),
+                            oa["sf_mma"].view(torch.float8_e4m3fn),
+                            F.ScalingType.BlockWise1x16,
+                            ow["sf_mma"].view(torch.float8_e4m3fn),
+                            F.ScalingType.BlockWise1x16,
+                            swizzle_a=F.SwizzleType.SWIZZLE_32_4_4,
+                            swizzle_b=F.SwizzleType.SWIZZLE_32_4_4,
+                            output_dtype=torch.bfloat16))
+    del sa, sw, oa, ow
+
+    # C1 block FP8 (1 x 128 activation scales, 128 x 128 weight scales)
+    r = bb.Float8BlockScaling(block_k=128)
+    sa = bb.cast(torch.randn(2048, 7168, generator=g, device=dev), r)
+    sw = bb.cast(torch.randn(4096, 7168, generator=g, device=dev) * 0.02, r, block_m=128)
+    run("c1_block_fp8", 2048, 4096, 7168,
+        lambda: bb.linear(sa, sw, out_dtype=torch.bfloat16),
+        lambda: F.scaled_mm(sa.data, sw.data.t(), sa.scale.t().contiguous().t(),
+                            F.ScalingType.BlockWise1x128, sw.scale,
+                            F.ScalingType.BlockWise128x128, output_dtype=torch.bfloat16))
+    del sa, sw
+    torch.cuda.empty_cache()
+    out["note"] = ("library GEMMs on the same operands, outside the product path; "
+                   "ms vs ours_ms_same_operands compares the two on this box")
+    return out
 
 
 # --------------------------------------------------------------- ncu cases
@@ -673,12 +1060,14 @@ NCU_CASES = {
     "gemm_nvfp4": "NVFP4 GEMM 8192x16384x8192 -> bf16",
     "gemm_block": "block-FP8 GEMM 2048x4096x7168 (C1) -> f32",
     "gemv_int4": "INT4 skinny GEMM M=1, W^T 28672x8192 (C5) -> bf16",
+    "gemv_int4_m16": "INT4 skinny GEMM M=16, W^T 28672x8192 (C5) -> bf16",
     "cast_pertensor": "per-tensor E4M3 cast, bf16 16384x8192 (amax + apply)",
     "cast_mxfp8": "MXFP8 cast, bf16 8192x8192",
     "cast_nvfp4": "NVFP4 cast, bf16 8192x8192",
     "cast_int4": "INT4 asym g128 cast, f32 8192x8192",
     "cast_block2d": "128x128 block FP8 cast, f32 4096x7168",
     "requant_nv_mx": "NVFP4 -> MXFP8 requantize, 8192x8192",
+    "dequant_mxfp8": "MXFP8 dequantize to f32, 8192x8192",
 }
 
 
@@ -703,14 +1092,17 @@ def run_ncu_case(name):
         a = bb.cast(torch.randn(2048, 7168, generator=g, device=dev), r)
         w = bb.cast(torch.randn(4096, 7168, generator=g, device=dev) * 0.02, r, block_m=128)
         fn = lambda: bb.linear(a, w, out_dtype=torch.float32)  # noqa: E731
-    elif name == "gemv_int4":
+    elif name.startswith("gemv_int4"):
         r = bb.INT4Scaling(group_size=128, signed=False, symmetric=False)
         w = bb.cast(torch.randn(28672, 8192, generator=g, device=dev) * 0.02, r)
-        a = bf16(1, 8192)
+        a = bf16(16 if name.endswith("m16") else 1, 8192)
         fn = lambda: bb.linear(a, w, out_dtype=torch.bfloat16)  # noqa: E731
     elif name == "requant_nv_mx":
         st = bb.cast(bf16(8192, 8192), bb.NVFP4BlockScaling())
         fn = lambda: bb.requantize(st, bb.MXFP8BlockScaling())  # noqa: E731
+    elif name == "dequant_mxfp8":
+        st = bb.cast(bf16(8192, 8192), bb.MXFP8BlockScaling())
+        fn = lambda: bb.dequantize(st)  # noqa: E731
     else:
         x, r, kw = {
             "cast_pertensor": (lambda: bf16(16384, 8192), bb.Float8CurrentScaling(), {}),

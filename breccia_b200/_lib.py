@@ -55,6 +55,7 @@ PROTOTYPES = {
     "brc_gemm_block_fp8": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_int4": ([_p, _i, _i, _p, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_status": ([_i], _i),
+    "brc_selftest_wait_timeout": ([_i, _p, _p], _i),
 }
 
 # status codes (include/breccia_b200.h)

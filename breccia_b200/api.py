@@ -88,19 +88,57 @@ def _ptr(t: Optional[torch.Tensor]):
 
 # Side data the tensor-core GEMMs consume (scales in the tcgen05 layout,
 # packed FP4/INT4 nibbles), keyed by the identity of a ScaledTensor's data
-# tensor and dropped when that tensor is freed.
+# tensor and dropped when that tensor is freed. Each entry carries a tag of
+# the data, scale and zero-point tensors' addresses and version counters
+# (torch bumps a tensor's version on every in-place write: copy_, index
+# assignment, out= ops), so codes or scales rewritten in place after the
+# cast make the entry stale; stale entries are never returned, and
+# ``_side_of`` rebuilds them from the current codes and scales on the GPU.
 _SIDE: dict = {}
 
 
-def _remember(data: torch.Tensor, **side) -> None:
+def _tag(data: torch.Tensor, companions=()) -> tuple:
+    tag = [data.data_ptr(), data._version]
+    for t in companions:
+        if isinstance(t, torch.Tensor):
+            tag += [t.data_ptr(), t._version]
+        else:
+            tag += [None, None]
+    return tuple(tag)
+
+
+def _remember(data: torch.Tensor, companions=(), **side) -> None:
     key = id(data)
-    if key not in _SIDE:
+    ent = _SIDE.get(key)
+    if ent is None:
         weakref.finalize(data, _SIDE.pop, key, None)
-    _SIDE.setdefault(key, {}).update(side)
+        ent = _SIDE[key] = {}
+    tag = _tag(data, companions)
+    if ent.get("_tag") != tag:
+        ent.clear()
+    ent.update(side)
+    ent["_tag"] = tag
 
 
-def _side(data: torch.Tensor) -> dict:
-    return _SIDE.get(id(data), {})
+def _side(data: torch.Tensor, companions=()) -> dict:
+    ent = _SIDE.get(id(data))
+    if not ent or ent.get("_tag") != _tag(data, companions):
+        return {}
+    return ent
+
+
+def _companions(scaled) -> tuple:
+    return (scaled.scale, getattr(scaled, "zero_point", None))
+
+
+def _side_of(scaled, rebuild: bool = True) -> dict:
+    """Current side data of a CUDA ScaledTensor; rebuilt from its codes and
+    scales when missing or stale (``attach_gemm_operands``)."""
+    side = _side(scaled.data, _companions(scaled))
+    if not side and rebuild:
+        attach_gemm_operands(scaled)
+        side = _side(scaled.data, _companions(scaled))
+    return side
 
 
 def _mma_scale_shape(rows: int, scale_cols: int):
@@ -193,7 +231,7 @@ def _cast_mxfp8(x, recipe, ST, L, st):
     sf_mma = torch.zeros(_mma_scale_shape(rows, K // 32), dtype=torch.uint8, device=x.device)
     _lib.call("brc_cast_mxfp8", x.data_ptr(), _IN_DT[x.dtype], rows, K, _FMT[fmt],
               codes.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
-    _remember(codes, sf_mma=sf_mma)
+    _remember(codes, (scale, None), sf_mma=sf_mma)
     return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockMN(block_m=1, block_n=32))
 
 
@@ -206,7 +244,7 @@ def _cast_nvfp4(x, recipe, ST, L, st):
     sf_mma = torch.zeros(_mma_scale_shape(rows, K // 16), dtype=torch.uint8, device=x.device)
     _lib.call("brc_cast_nvfp4", x.data_ptr(), _IN_DT[x.dtype], rows, K, codes.data_ptr(),
               packed.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
-    _remember(codes, packed=packed, sf_mma=sf_mma)
+    _remember(codes, (scale, None), packed=packed, sf_mma=sf_mma)
     return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockMN(block_m=1, block_n=16))
 
 
@@ -231,7 +269,8 @@ def _cast_int4(x, recipe, ST, L, st):
               codes.data_ptr(), None, scale.data_ptr(), _ptr(zp), _ptr(tiles), _ptr(stiles),
               _ptr(ztiles), st)
     if tiles is not None:
-        _remember(codes, int4_tiles=tiles, int4_scale_tiles=stiles, int4_zp_tiles=ztiles)
+        _remember(codes, (scale, zp), int4_tiles=tiles, int4_scale_tiles=stiles,
+                  int4_zp_tiles=ztiles)
     return ST(data=codes, scale=scale, recipe=recipe, layout=L.PerBlockK(block_size=G),
               zero_point=zp)
 
@@ -317,7 +356,7 @@ def requantize(scaled, recipe):
             _lib.call("brc_requant_nvfp4_to_mxfp8", codes.data_ptr(),
                       _aligned(scaled.scale).data_ptr(), rows, K, _FMT[recipe.fp8_format],
                       out.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), _stream(dev))
-        _remember(out, sf_mma=sf_mma)
+        _remember(out, (scale, None), sf_mma=sf_mma)
         return ST(data=out, scale=scale, recipe=recipe,
                   layout=L.PerBlockMN(block_m=1, block_n=32))
     return cast(dequantize(scaled), recipe)
@@ -370,7 +409,8 @@ def attach_gemm_operands(scaled):
     if name not in ("nvfp4", "mxfp8", "int4") or not isinstance(data, torch.Tensor) \
             or not data.is_cuda or data.ndim < 1:
         return scaled
-    side = _side(data)
+    comp = _companions(scaled)
+    side = _side(data, comp)
     dev = data.device
     codes = _aligned(data.contiguous().view(torch.uint8))
     K = codes.shape[-1]
@@ -393,7 +433,7 @@ def attach_gemm_operands(scaled):
                           packed.data_ptr(), st)
                 add["packed"] = packed
             if add:
-                _remember(data, **add)
+                _remember(data, comp, **add)
         elif "int4_tiles" not in side and scaled.recipe.group_size == 128 and \
                 rows % 16 == 0 and K % 128 == 0:
             sc = _aligned(scaled.scale.contiguous())
@@ -407,7 +447,8 @@ def attach_gemm_operands(scaled):
             ztiles = None if zp is None else torch.empty_like(stiles)
             _lib.call("brc_int4_tiles", codes.data_ptr(), rows, K, sc.data_ptr(), _ptr(zp),
                       sdt, tiles.data_ptr(), stiles.data_ptr(), _ptr(ztiles), st)
-            _remember(data, int4_tiles=tiles, int4_scale_tiles=stiles, int4_zp_tiles=ztiles)
+            _remember(data, comp, int4_tiles=tiles, int4_scale_tiles=stiles,
+                      int4_zp_tiles=ztiles)
     return scaled
 
 
@@ -416,5 +457,5 @@ def gemm_operands(scaled) -> dict:
     the tcgen05 layout), ``packed`` (two 4-bit codes per byte, element 2i in
     the low nibble), or the INT4 skinny-GEMM tiles (``int4_tiles``,
     ``int4_scale_tiles``, ``int4_zp_tiles``)."""
-    return dict(_side(scaled.data if scaled.data.dtype == torch.uint8
-                      else scaled.data))
+    side = _side(scaled.data, _companions(scaled))
+    return {k: v for k, v in side.items() if not k.startswith("_")}

@@ -210,7 +210,7 @@ def load_safetensors(path: str, *, device: Any = None) -> Dict[str, Any]:
                     zero_point=f.get_tensor(zp_key) if zp_key in keys else None)
             if dev is not None:
                 if lo is not None and recipe.name == "nvfp4":
-                    _remember(st.data, packed=lo)
+                    _remember(st.data, (st.scale, st.zero_point), packed=lo)
                 attach_gemm_operands(st)
             out[name] = st
     return out

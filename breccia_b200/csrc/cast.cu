@@ -1693,7 +1693,9 @@ __global__ void __launch_bounds__(1024) k_reduce_partials(const uint32_t* partia
 namespace {
 // Device address of the scratch array, looked up once per device with that
 // device current. In host code `g_scratch` names a host-side shadow, not the
-// device array, so kernels must be given this address.
+// device array, so kernels must be given this address. The address is cached
+// for the life of the process; a device reset after the first call would
+// leave it stale, which the header documents as unsupported.
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 uint32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};

@@ -1259,6 +1259,53 @@ using namespace brc::gemm;
 
 namespace {
 uint32_t* status_word() { return brc::gemm_status_ptr(); }
+
+// ------------------------------------------------------------------ failure-path self-test
+// The GEMMs' failure path, run on purpose without a fault: one CTA sets up
+// as the GEMMs do (barriers, a TMEM allocation), warp 0 waits on a barrier
+// nothing ever arrives at with a short bound, and warp 1 waits on another
+// with the GEMMs' normal 2 s bound. Warp 0's wait runs out, records the
+// timeout in the status word and raises the CTA's abort flag; warp 1 must
+// leave on that flag well before its own bound. Both then take the GEMMs'
+// tear-down (fences, CTA barrier, TMEM freed by the warp that allocated it).
+// Bit w of g_selftest_roles is set when warp w left its wait without the
+// barrier completing.
+__device__ uint32_t g_selftest_roles = 0;
+
+__global__ void __launch_bounds__(64, 1) k_selftest_wait_timeout(uint64_t limit_ns,
+                                                                 uint32_t* status) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ uint32_t abort_word;
+  volatile uint32_t* abort_flag = &abort_word;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const bool done = warp == 0
+                        ? __all_sync(0xffffffffu, mbar_wait(&bars[0], 0u, abort_flag, status, 1u,
+                                                            limit_ns))
+                        : __all_sync(0xffffffffu, mbar_wait(&bars[1], 0u, abort_flag, status, 1u));
+  if (lane == 0 && !done) atomicOr(&g_selftest_roles, 1u << warp);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
 }  // namespace
 
 extern "C" {
@@ -1420,6 +1467,26 @@ int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, 
   if (a_fmt == BRC_FP8_E4M3) return launch_block_out<0, 1>(d_dtype, ta, tb, p, st);
   if (b_fmt == BRC_FP8_E4M3) return launch_block_out<1, 0>(d_dtype, ta, tb, p, st);
   return launch_block_out<1, 1>(d_dtype, ta, tb, p, st);
+}
+
+int brc_selftest_wait_timeout(int limit_us, int* roles_out, void* stream) {
+  if (limit_us <= 0 || limit_us > 1000000) return BRC_ERR_RANGE;
+  uint32_t* status = status_word();
+  if (!status) return BRC_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t zero = 0;
+  int rc = check_cuda(cudaMemcpyToSymbolAsync(g_selftest_roles, &zero, sizeof(zero), 0,
+                                              cudaMemcpyHostToDevice, st));
+  if (rc) return rc;
+  k_selftest_wait_timeout<<<1, 64, 0, st>>>((uint64_t)limit_us * 1000ull, status);
+  if ((rc = check_launch())) return rc;
+  if ((rc = check_cuda(cudaStreamSynchronize(st)))) return rc;
+  uint32_t roles = 0, st_word = 0;
+  if ((rc = check_cuda(cudaMemcpyFromSymbol(&roles, g_selftest_roles, sizeof(roles))))) return rc;
+  if ((rc = check_cuda(cudaMemcpyFromSymbol(&st_word, g_gemm_status, sizeof(st_word)))))
+    return rc;
+  if (roles_out) *roles_out = (int)roles;
+  return (st_word & 1u) ? BRC_ERR_TIMEOUT : BRC_OK;
 }
 
 int brc_gemm_status(int reset) {

@@ -91,13 +91,13 @@ constexpr uint32_t kSleepHintNs = 20000;          // re-check abort / deadline e
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile uint32_t* abort_flag, uint32_t* status,
-                                          uint32_t code) {
+                                          uint32_t code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, kSleepHintNs)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1u;
       if (status) atomicOr(status, code);
       return false;

@@ -3,13 +3,14 @@
 The reference is single-process; these helpers are the multi-GPU form of its
 hot path. Two layouts use them.
 
-Data parallel (bench.py's default for N > 1): each rank holds its own batch of
+Data parallel (bench.py --shard batch): each rank holds its own batch of
 activation rows and the whole weight. The activations' per-tensor scale is the
 one of the concatenated batch, so the local amax words are all-reduced; the
 weight's cast is local. ``cast_per_tensor_async`` lets that all-reduce overlap
 the weight's cast.
 
-Weight split: weights are split along N (the output dimension): each rank holds
+Weight split (bench.py's default for N > 1, ``cast_weight_split``): weights are
+split along N (the output dimension): each rank holds
 ``W^T[n0:n1, :]`` (rows of the nn.Linear-oriented weight), casts it, and
 computes ``C[:, n0:n1] = A @ W^T[n0:n1, :]^T``. Block recipes need no
 communication (their blocks run along K, inside one rank's rows). Per-tensor
@@ -30,7 +31,7 @@ from . import _lib
 from .api import _input, _classes, _stream, _IN_DT, _FMT, _TORCH_FP8
 
 __all__ = ["shard_rows", "allreduce_amax_word", "cast_per_tensor_sharded", "cast_sharded",
-           "cast_per_tensor_async", "PendingCast"]
+           "cast_per_tensor_async", "PendingCast", "cast_weight_split"]
 
 
 def shard_rows(n: int, world: int, rank: int, align: int = 128):
@@ -40,6 +41,12 @@ def shard_rows(n: int, world: int, rank: int, align: int = 128):
     per = -(-per // align) * align
     lo = min(n, rank * per)
     return lo, min(n, lo + per)
+
+
+def _world(group=None):
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(group), dist.get_rank(group)
+    return 1, 0
 
 
 def allreduce_amax_word(word: torch.Tensor, group=None) -> torch.Tensor:
@@ -118,3 +125,53 @@ def cast_sharded(x_shard, recipe, group=None, **kw):
     if getattr(recipe, "name", None) in ("delayed", "current"):
         return cast_per_tensor_sharded(x_shard, recipe, group)
     return cast(x_shard, recipe, **kw)
+
+
+def cast_weight_split(a, w_shard, recipe, group=None, **kw):
+    """Operands of one layer in the weight-split layout: ``a`` is the whole
+    activation (replicated: every rank holds all of it), ``w_shard`` this
+    rank's rows ``[n0, n1)`` of ``W^T``. Returns ``(cast(a), cast(w_shard))``
+    equal, bit for bit, to the single-GPU casts of ``a`` and of the rows
+    ``[n0, n1)`` of the whole weight.
+
+    Per-tensor recipes need two global amaxes: the activation's (over all its
+    rows) and the weight's (over every rank's shard). Each rank reduces only
+    its ``1/world`` share of the activation's rows (``shard_rows``) and its
+    weight shard into two 32-bit words, ONE all-reduce(MAX) of those 8 bytes
+    gives both global amaxes, and each rank then encodes the whole activation
+    and its shard. The activation's amax pass thus shrinks with the number of
+    ranks; its encode pass does not (every rank needs all of its codes).
+    Block recipes are rank-local (their blocks run along K)."""
+    from .api import cast
+    if getattr(recipe, "name", None) not in ("delayed", "current"):
+        return cast(a, recipe, **kw), cast(w_shard, recipe, **kw)
+    x, w = _input(a), _input(w_shard)
+    world, rank = _world(group)
+    K = x.shape[-1] if x.ndim else 1
+    rows = x.numel() // K if K else 0
+    lo, hi = shard_rows(rows, world, rank)
+    dev = x.device
+    words = torch.empty(2, dtype=torch.int32, device=dev)
+    fmt = recipe.fp8_format
+    ST, L = _classes(recipe)
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        _lib.call("brc_amax_reset", words.data_ptr(), st)
+        _lib.call("brc_amax_reset", words.data_ptr() + 4, st)
+        _lib.call("brc_amax_accumulate", x.data_ptr() + lo * K * x.element_size(),
+                  _IN_DT[x.dtype], (hi - lo) * K, words.data_ptr(), st)
+        _lib.call("brc_amax_accumulate", w.data_ptr(), _IN_DT[w.dtype], w.numel(),
+                  words.data_ptr() + 4, st)
+    if world > 1:
+        dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group)
+    out = []
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        for t, off in ((x, 0), (w, 4)):
+            codes = torch.empty(t.shape, dtype=torch.uint8, device=dev)
+            scale = torch.empty((), dtype=torch.float32, device=dev)
+            _lib.call("brc_cast_pertensor_fp8_apply", t.data_ptr(), _IN_DT[t.dtype], t.numel(),
+                      _FMT[fmt], words.data_ptr() + off, codes.data_ptr(), scale.data_ptr(), st)
+            out.append(ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe,
+                          layout=L.PerTensor()))
+    return out[0], out[1]

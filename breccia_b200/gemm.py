@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .api import (dequantize, _is_scaled, _require_cuda, _side, _codes_u8, _stream, _FMT,
+from .api import (dequantize, _is_scaled, _require_cuda, _side_of, _codes_u8, _stream, _FMT,
                   _OUT_DT)
 
 _PER_TENSOR = ("delayed", "current")
@@ -68,7 +68,7 @@ def _tc_pair(a, w):
         if a.scale.ndim == 0 and w.scale.ndim == 0:
             return "fp8"
     if na == "mxfp8" and nw == "mxfp8" and K % 128 == 0:
-        if "sf_mma" in _side(a.data) and "sf_mma" in _side(w.data):
+        if "sf_mma" in _side_of(a) and "sf_mma" in _side_of(w):
             return "mxfp8"
     if na == "block" and nw == "block" and K % 128 == 0 and \
             a.recipe.block_k == 128 and w.recipe.block_k == 128:
@@ -77,7 +77,7 @@ def _tc_pair(a, w):
                 w.layout.block_n == 128:
             return "block"
     if na == "nvfp4" and nw == "nvfp4" and K % 256 == 0:
-        sa, sw = _side(a.data), _side(w.data)
+        sa, sw = _side_of(a), _side_of(w)
         if "sf_mma" in sa and "packed" in sa and "sf_mma" in sw and "packed" in sw:
             return "nvfp4"
     return None
@@ -95,7 +95,7 @@ def _int4_pair(a, w):
     M = a.numel() // K if K else 0
     N = w.data.shape[0]
     return (w.data.shape[1] == K and 0 < M <= 16 and K % 1024 == 0 and N % 16 == 0 and
-            w.recipe.group_size == 128 and "int4_tiles" in _side(w.data))
+            w.recipe.group_size == 128 and "int4_tiles" in _side_of(w))
 
 
 def _run_int4(a, w, out_dtype):
@@ -109,7 +109,7 @@ def _run_int4(a, w, out_dtype):
     if a2.data_ptr() % 16:
         a2 = a2.clone()
     r = w.recipe
-    side = _side(w.data)
+    side = _side_of(w)
     zt = side["int4_zp_tiles"]
     with torch.cuda.device(dev):
         _lib.call("brc_gemm_int4", a2.data_ptr(), M, K, side["int4_tiles"].data_ptr(), N,
@@ -141,13 +141,13 @@ def _run_tc(kind, a, w, out_dtype, w_codes=None):
                       _FMT[w.recipe.fp8_format], a.scale.contiguous().data_ptr(),
                       w.scale.contiguous().data_ptr(), out.data_ptr(), _OUT_DT[cdt], st)
         elif kind == "mxfp8":
-            sa, sw = _side(a.data), _side(w.data)
+            sa, sw = _side_of(a), _side_of(w)
             _lib.call("brc_gemm_mxfp8", _codes_u8(a.data).data_ptr(), _codes_u8(w.data).data_ptr(),
                       M, N, K, _FMT[a.recipe.fp8_format], _FMT[w.recipe.fp8_format],
                       sa["sf_mma"].data_ptr(), sw["sf_mma"].data_ptr(), out.data_ptr(),
                       _OUT_DT[cdt], st)
         else:
-            sa, sw = _side(a.data), _side(w.data)
+            sa, sw = _side_of(a), _side_of(w)
             _lib.call("brc_gemm_nvfp4", sa["packed"].data_ptr(), sw["packed"].data_ptr(), M, N, K,
                       sa["sf_mma"].data_ptr(), sw["sf_mma"].data_ptr(), out.data_ptr(),
                       _OUT_DT[cdt], st)

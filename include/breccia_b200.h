@@ -88,7 +88,10 @@ int brc_cast_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt, uint8
  * library, held until exit), so n is limited to 536,870,912 elements
  * (16384 chunks of 32768); larger inputs return BRC_ERR_RANGE. The first call
  * on a device looks up the scratch address on the current device; make that
- * first call before any stream capture. All calls on a device share the
+ * first call before any stream capture. The address is kept for the life of
+ * the process, so resetting that device (cudaDeviceReset) after the first
+ * call is not supported: later calls would hand the kernels a stale address.
+ * All calls on a device share the
  * scratch: calls whose kernels overlap on the GPU race and must be
  * serialised by the caller. Each call rewrites every scratch slot it reads. */
 int brc_cast_pertensor_fp8_noalloc(const void* x, int x_dtype, int64_t n, int fmt,
@@ -293,8 +296,21 @@ int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_tiles, int 
                   int symmetric, const float* scale_tiles, const float* zp_tiles, void* d,
                   int d_dtype, void* stream);
 /* Sticky device status of the GEMM kernels on the current device (bit 0: a
- * bounded wait timed out and the kernel returned early). Synchronous. */
+ * bounded wait timed out and the kernel returned early). Synchronous. The
+ * status word's address is looked up once per device and kept for the life
+ * of the process (a device reset after the first GEMM is not supported). */
 int brc_gemm_status(int reset);
+/* Failure-path self-test (no counterpart in the reference; the reference has
+ * no device code). Runs the GEMMs' bounded-wait and tear-down code in one CTA
+ * against a barrier nothing arrives at: one role waits with a `limit_us`
+ * bound (1 .. 1,000,000 us, else BRC_ERR_RANGE), a second role waits with
+ * the GEMMs' normal 2 s bound and must leave on the first role's abort flag;
+ * TMEM is allocated and freed as in the GEMMs. No fault, trap or unbounded
+ * wait is involved. Synchronous on `stream`. Returns BRC_ERR_TIMEOUT when the
+ * timeout was recorded in the GEMM status word (the expected outcome; the
+ * bit stays set until brc_gemm_status(1)); `roles_out` (optional) receives a
+ * bit per role that left its wait without the barrier completing (3 = both). */
+int brc_selftest_wait_timeout(int limit_us, int* roles_out, void* stream);
 
 /* ======================================================= diagnostics
  * Writes, for each i, the float32 quotient x[i] / s[i] as the cast kernels

@@ -86,10 +86,14 @@ def _rows2d(x):
     return x.reshape(-1, x.shape[-1]) if x.ndim >= 1 else x.reshape(1, 1)
 
 
-def cast_per_tensor_fp8(x, recipe, literal=False, chunk_rows=4096) -> Q:
-    """``cast.py:364-373``: float64 tensor amax -> float32 scale -> encode."""
+def cast_per_tensor_fp8(x, recipe, literal=False, chunk_rows=4096, amax=None) -> Q:
+    """``cast.py:364-373``: float64 tensor amax -> float32 scale -> encode.
+
+    ``amax`` (test helper): the ``tensor_amax`` of a larger tensor of which
+    ``x`` is a row subset, so sampled rows of a full-size tensor encode with
+    the full tensor's scale, as they do inside it."""
     fmt = recipe.fp8_format
-    amax = codec.tensor_amax(x)
+    amax = codec.tensor_amax(x) if amax is None else amax
     scale_dequant = np.float32(amax / _fmt_max(fmt))
     x2 = _rows2d(x)
     data = _chunked_encode(lambda a, b: x2[a:b] / scale_dequant, x2.shape[0],

@@ -388,8 +388,17 @@ def _config_inputs(name):
         m = torch.rand(16384, 8192, generator=g) < 0.001
         a[m] = torch.randn(int(m.sum()), generator=g) * 50
         return a.to(torch.bfloat16)
+    if name == "c1_Wt":
+        torch.randn(2048, 7168, generator=g)  # A comes first in the config
+        return torch.randn(4096, 7168, generator=g) * 0.02
+    if name == "c2_Wt":
+        return (torch.randn(8192, 8192, generator=g) * 0.02).to(torch.bfloat16)
     if name == "c3_A":
         return torch.randn(8192, 8192, generator=g).to(torch.bfloat16)
+    if name == "c3_Wt":
+        return (torch.randn(28672, 8192, generator=g) * 0.02).to(torch.bfloat16)
+    if name == "c4_A":
+        return torch.randn(4096, 8192, generator=g).to(torch.bfloat16)
     if name == "c4_Wt":
         w = torch.distributions.StudentT(4.0).sample((28672, 8192)) * 0.02
         return w.to(torch.bfloat16)
@@ -399,8 +408,9 @@ def _config_inputs(name):
 
 
 @pytest.mark.parametrize("cfg,rname", [
-    ("c1_A", "block128"), ("c2_A", "current_e4m3"), ("c3_A", "mxfp8"),
-    ("c4_Wt", "nvfp4"), ("c5_Wt", "int4_asym"),
+    ("c1_A", "block128"), ("c2_A", "current_e4m3"), ("c2_Wt", "current_e4m3"),
+    ("c3_A", "mxfp8"), ("c3_Wt", "mxfp8"), ("c4_A", "nvfp4"), ("c4_Wt", "nvfp4"),
+    ("c5_Wt", "int4_asym"),
 ])
 def test_full_size_sampled_rows(cfg, rname):
     from oracle import cast as ocast, codec
@@ -423,3 +433,19 @@ def test_full_size_sampled_rows(cfg, rname):
     assert same_bits(_np(st.scale[rows]), q.scale)
     if q.zero_point is not None:
         assert same_bits(_np(st.zero_point[rows]), q.zero_point)
+
+
+def test_full_size_block128x128_weight():
+    """C1 W^T f32 (4096, 7168) with 128 x 128 tiles (the DeepSeek-v3 weight
+    layout, restated oracle): sampled 128-row bands, codes and tile scales."""
+    from oracle import cast as ocast
+    r = _recipes()["block128"]
+    x = _config_inputs("c1_Wt")
+    st = bb().cast(x.cuda(), r, block_m=128)
+    assert tuple(st.scale.shape) == (4096 // 128, 7168 // 128)
+    for band in (0, 13, 31):
+        xs = x[128 * band: 128 * (band + 1)].numpy()
+        q = ocast.cast_block_fp8_2d(xs, r, block_m=128)
+        data = _np(st.data[128 * band: 128 * (band + 1)])
+        assert same_bits(data, q.data), _first_diff(data, q.data)
+        assert same_bits(_np(st.scale[band: band + 1]), q.scale)

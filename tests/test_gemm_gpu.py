@@ -279,3 +279,115 @@ def test_int4_weight_only_config5_shape():
     qw = ocast.cast(Wt[cols].numpy(), r)
     ref = ocast.matmul(A.float().numpy(), ocast.dequantize(qw).T)
     _check(out[:, cols], ref)
+
+
+# ------------------------------------------------ shapes the benchmark times
+# The CTA-pair kernels stream K through a 5-7 stage shared-memory ring and a
+# cluster walks several 256 x 256 tiles; these cases wrap the ring many times
+# (K = 2048: 16 K blocks, K = 8192: 64) with several tiles per cluster, at
+# the BASELINE config shapes themselves. The output is checked on a sample of
+# rows and columns (the first and last, tile edges, random ones) against the
+# reference's matmul of the oracle's casts of those rows.
+
+
+def _pick(n, k, seed):
+    g = np.random.default_rng(seed)
+    edges = [i for i in (0, 127, 128, 255, 256, n // 2, n - 129, n - 128, n - 1) if 0 <= i < n]
+    return np.unique(np.concatenate([edges, g.choice(n, size=min(k, n), replace=False)]))
+
+
+def _oracle_sample(A, W, r, rows, cols):
+    """Reference matmul of A[rows] @ W[cols]^T (W given as (N, K)). Block
+    recipes are row-independent, so the sampled rows cast alone equal their
+    rows of the full cast; per-tensor recipes encode them with the amax of
+    the whole tensor (``cast.py:364-373``)."""
+    from oracle import cast as ocast, codec
+    a, w = A[rows].float().numpy(), W[cols].float().numpy()
+    if r.name in ("delayed", "current"):
+        qa = ocast.cast_per_tensor_fp8(a, r, amax=codec.tensor_amax(A.abs().max().float().numpy()))
+        qw = ocast.cast_per_tensor_fp8(w, r, amax=codec.tensor_amax(W.abs().max().float().numpy()))
+    else:
+        qa, qw = ocast.cast(a, r), ocast.cast(w, r)
+    return ocast.matmul(qa, ocast.dequantize(qw).T)
+
+
+def _gemm_sampled(A, W, r, rows, cols, out_dtype=torch.bfloat16):
+    from breccia_b200 import gemm
+    sa, sw = bb().cast(A.cuda(), r), bb().cast(W.cuda(), r)
+    assert gemm._tc_pair(sa, sw) is not None
+    out = bb().linear(sa, sw, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert _gemm_status() == 0
+    got = out[torch.as_tensor(rows).cuda()][:, torch.as_tensor(cols).cuda()].float().cpu().numpy()
+    del sa, sw, out
+    return got
+
+
+@pytest.mark.parametrize("kind", ["current", "delayed_e5m2", "mxfp8", "mxfp8_e5m2", "nvfp4"])
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 8192), (4096, 4864, 2048), (2304, 2320, 8192)])
+def test_cta_pair_long_k(kind, M, N, K):
+    """CTA-pair path (at least 74 tiles of 256 x 256) with 16 or 64 K blocks,
+    ragged M and N, float32 output."""
+    from breccia_b200 import _lib
+    assert _lib.lib() is not None
+    assert ((M + 255) // 256) * ((N + 255) // 256) >= torch.cuda.get_device_properties(
+        0).multi_processor_count // 2
+    r = _recipe(kind)
+    A, W = _operands(M, N, K, seed=M + N + K + 11, heavy=(kind == "nvfp4"))
+    rows, cols = _pick(M, 80, 1), _pick(N, 200, 2)
+    got = _gemm_sampled(A, W, r, rows, cols, out_dtype=torch.float32)
+    _check(got, _oracle_sample(A, W, r, rows, cols), tight=1e-5)
+
+
+def _config_operands(cfg):
+    """BASELINE.json configs[1..3] as seeded CPU tensors: A (M, K), W^T (N, K)."""
+    g = torch.Generator().manual_seed(0)
+    if cfg == "c2":
+        A = torch.randn(16384, 8192, generator=g)
+        m = torch.rand(16384, 8192, generator=g) < 0.001
+        A[m] = torch.randn(int(m.sum()), generator=g) * 50
+        W = torch.randn(8192, 8192, generator=g) * 0.02
+        return A.to(torch.bfloat16), W.to(torch.bfloat16), "current"
+    if cfg == "c3":
+        A = torch.randn(8192, 8192, generator=g).to(torch.bfloat16)
+        W = (torch.randn(28672, 8192, generator=g) * 0.02).to(torch.bfloat16)
+        return A, W, "mxfp8"
+    A = torch.randn(4096, 8192, generator=g).to(torch.bfloat16)
+    torch.manual_seed(4)
+    W = (torch.distributions.StudentT(4.0).sample((28672, 8192)) * 0.02).to(torch.bfloat16)
+    return A, W, "nvfp4"
+
+
+@pytest.mark.parametrize("cfg", ["c2", "c3", "c4"])
+def test_config_shape_gemm(cfg):
+    """The GEMMs bench.py times, at full size with bf16 output: C2 per-tensor
+    E4M3 16384 x 8192 x 8192, C3 MXFP8 8192 x 28672 x 8192, C4 NVFP4
+    4096 x 28672 x 8192 (Student-t weights)."""
+    A, W, kind = _config_operands(cfg)
+    r = _recipe(kind)
+    rows, cols = _pick(A.shape[0], 64, 3), _pick(W.shape[0], 400, 4)
+    got = _gemm_sampled(A, W, r, rows, cols)
+    _check(got, _oracle_sample(A, W, r, rows, cols))
+
+
+@pytest.mark.parametrize("kind", ["mxfp8", "nvfp4"])
+def test_in_place_rewrite_of_operands(kind):
+    """Codes and scales written into an existing ScaledTensor in place (a
+    reused weight buffer) must reach the tensor-core GEMM: the packed codes
+    and scale atoms recorded at cast time are stale then and are rebuilt."""
+    from breccia_b200 import gemm
+    r = _recipe(kind)
+    A, W1 = _operands(256, 512, 512, seed=21)
+    _, W2 = _operands(256, 512, 512, seed=22)
+    sa = bb().cast(A.cuda(), r)
+    sw = bb().cast(W1.cuda(), r)
+    first = bb().linear(sa, sw, out_dtype=torch.float32)
+    other = bb().cast(W2.cuda(), r)
+    sw.data.copy_(other.data)
+    sw.scale.copy_(other.scale)
+    assert gemm._tc_pair(sa, sw) == kind
+    got = bb().linear(sa, sw, out_dtype=torch.float32)
+    want = bb().linear(sa, other, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert not torch.equal(got, first)

@@ -34,19 +34,32 @@ def _input(rows, cols, seed, mag):
     return x.to(torch.bfloat16).cuda()
 
 
-def _cast(fn_name, x, lib, with_workspace):
+_DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _cast(fn_name, x, lib, with_workspace, fmt=0):
     codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
     scale = torch.empty((), dtype=torch.float32, device=x.device)
     stream = torch.cuda.current_stream().cuda_stream
+    xp = x.data_ptr() if x.numel() else 0
+    cp = codes.data_ptr() if x.numel() else 0
     if with_workspace:
         ws = torch.empty(1, dtype=torch.int32, device=x.device)
-        rc = getattr(lib, fn_name)(x.data_ptr(), 1, x.numel(), 0, codes.data_ptr(),
+        rc = getattr(lib, fn_name)(xp, _DT[x.dtype], x.numel(), fmt, cp,
                                    scale.data_ptr(), ws.data_ptr(), stream)
     else:
-        rc = getattr(lib, fn_name)(x.data_ptr(), 1, x.numel(), 0, codes.data_ptr(),
+        rc = getattr(lib, fn_name)(xp, _DT[x.dtype], x.numel(), fmt, cp,
                                    scale.data_ptr(), stream)
     assert rc == 0, lib.brc_status_string(rc)
     return codes, scale
+
+
+def _same(x, lib, fmt=0):
+    want_codes, want_scale = _cast("brc_cast_pertensor_fp8", x, lib, True, fmt)
+    got_codes, got_scale = _cast("brc_cast_pertensor_fp8_noalloc", x, lib, False, fmt)
+    torch.cuda.synchronize()
+    assert got_scale.view(torch.int32).item() == want_scale.view(torch.int32).item()
+    assert torch.equal(got_codes, want_codes)
 
 
 def test_noalloc_matches_allocating_cast_twice():
@@ -71,3 +84,31 @@ def test_noalloc_rejects_inputs_beyond_its_scratch():
     rc = lib.brc_cast_pertensor_fp8_noalloc(x.data_ptr(), 1, too_big, 0, out.data_ptr(),
                                             scale.data_ptr(), ctypes.c_void_p(None))
     assert rc == _lib.BRC_ERR_RANGE
+
+
+def test_noalloc_special_inputs():
+    """Edge cases with their own handling in the scratch kernels, each
+    compared bit for bit with the allocating cast: an empty input (no chunk
+    runs; the final amax word is written as 0 and the 1e-10 floor gives the
+    scale), a NaN (the per-chunk max propagates it, the reduction over float
+    bits keeps it), an infinity, all zeros, and lengths that are not a
+    multiple of the 16-byte vector (the last chunk takes the scalar loop),
+    in all three input dtypes and both FP8 formats. Runs after a large call,
+    so every slot read here was last written by another input."""
+    from breccia_b200 import _lib
+    lib = _lib.lib()
+    _same(_input(2048, 4096, 7, 100.0), lib)  # leaves large partials behind
+    _same(torch.empty(0, dtype=torch.bfloat16, device="cuda"), lib)
+    for dt in (torch.float32, torch.bfloat16, torch.float16):
+        for fmt in (0, 1):
+            g = torch.Generator().manual_seed(11)
+            base = torch.randn(3 * 32768 + 5, generator=g)
+            _same(base.to(dt).cuda(), lib, fmt)  # ragged tail chunk
+            x = base.clone()
+            x[40000] = float("nan")
+            _same(x.to(dt).cuda(), lib, fmt)
+            x = base.clone()
+            x[70001] = float("-inf")
+            _same(x.to(dt).cuda(), lib, fmt)
+            _same(torch.zeros(1000, dtype=dt, device="cuda"), lib, fmt)
+            _same(base[:7].to(dt).cuda(), lib, fmt)  # shorter than one vector
