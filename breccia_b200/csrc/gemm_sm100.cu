@@ -88,7 +88,9 @@ struct Smem {
   static constexpr uint32_t kSfA = kB + STAGES * B_BYTES;
   static constexpr uint32_t kSfB = kSfA + STAGES * SfCfg<KIND>::A_SF;
   static constexpr uint32_t kBar = kSfB + STAGES * SfCfg<KIND>::B_SF;
-  static constexpr uint32_t kNumBars = 4 * STAGES + 8;  // stage ring, scale-factor ring, accumulator/partial/drain
+  // operand ring (full, empty), scale-factor rings (loaded, in TMEM, slot free),
+  // accumulator / partial / drain barriers
+  static constexpr uint32_t kNumBars = 5 * STAGES + 8;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
@@ -173,8 +175,9 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
   uint64_t* sf_full = drain + 1;        // scale factors of a stage are in TMEM
   uint64_t* sf_free = sf_full + STAGES;  // the MMAs reading a stage's TMEM slot are done
   uint64_t* cdrain = sf_free + STAGES;
+  uint64_t* sf_loaded = cdrain + 1;     // a stage's scale atoms are in shared memory
   constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
-  static_assert(4 * STAGES + 4 <= L::kNumBars, "barrier area too small");
+  static_assert(5 * STAGES + 4 <= L::kNumBars, "barrier area too small");
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
 
@@ -193,6 +196,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sf_full[s], 1);
       mbar_init(&sf_free[s], 1);
+      mbar_init(&sf_loaded[s], 1);
     }
     mbar_init(cdrain, 1);
     *abort_flag = 0u;
@@ -226,24 +230,27 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
             ok = false;
             break;
           }
-          uint32_t bytes = A_BYTES + B_BYTES;
-          const bool b_hi = KIND != kPerTensor && (2 * nb + 1) < p.sfb_row_atoms;
-          if constexpr (KIND != kPerTensor) bytes += SF::A_SF + (b_hi ? SF::B_SF : SF::B_SF / 2);
-          mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d(smem + L::kA + stage * A_BYTES, &tmap_a, kb * BKB, mb * BM, &full[stage]);
-          tma_load_2d(smem + L::kB + stage * B_BYTES, &tmap_b, kb * BKB, nb * BN, &full[stage]);
+          // The scale atoms go first and complete on their own barrier, so
+          // their copies into TMEM can run while the operand tiles are
+          // still in flight instead of after them.
           if constexpr (KIND != kPerTensor) {
+            const bool b_hi = (2 * nb + 1) < p.sfb_row_atoms;
             const uint32_t kcol = (uint32_t)kb * SF::kAtomsK;
+            mbar_arrive_expect_tx(&sf_loaded[stage], SF::A_SF + (b_hi ? SF::B_SF : SF::B_SF / 2));
             bulk_load(smem + L::kSfA + stage * SF::A_SF,
-                      p.sfa + ((size_t)mb * p.sf_col_tiles + kcol) * 512, SF::A_SF, &full[stage]);
+                      p.sfa + ((size_t)mb * p.sf_col_tiles + kcol) * 512, SF::A_SF,
+                      &sf_loaded[stage]);
             bulk_load(smem + L::kSfB + stage * SF::B_SF,
                       p.sfb + ((size_t)(2 * nb) * p.sf_col_tiles + kcol) * 512, SF::B_SF / 2,
-                      &full[stage]);
+                      &sf_loaded[stage]);
             if (b_hi)
               bulk_load(smem + L::kSfB + stage * SF::B_SF + SF::B_SF / 2,
                         p.sfb + ((size_t)(2 * nb + 1) * p.sf_col_tiles + kcol) * 512,
-                        SF::B_SF / 2, &full[stage]);
+                        SF::B_SF / 2, &sf_loaded[stage]);
           }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(smem + L::kA + stage * A_BYTES, &tmap_a, kb * BKB, mb * BM, &full[stage]);
+          tma_load_2d(smem + L::kB + stage * B_BYTES, &tmap_b, kb * BKB, nb * BN, &full[stage]);
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -258,6 +265,10 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           if (issued & (1u << s)) {
             const uint64_t t0 = globaltimer();
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+            while (KIND != kPerTensor &&
+                   !mbar_try_wait(&sf_loaded[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
           }
@@ -303,8 +314,13 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&sf_loaded[stage], phase, abort_flag, p.status, 1u))) {
+              ok = false;
+              break;
+            }
           }
-          if (lane == 0) {
+          if (elect_lane()) {
             if constexpr (!kCopier && KIND != kPerTensor) {
               const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
               const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
@@ -342,12 +358,12 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           }
         }
         if (!ok) break;
-        if (lane == 0) tc_commit(tmem_full);
+        if (elect_lane()) tc_commit(tmem_full);
         __syncwarp();
         acc_phase ^= 1u;
       }
       // every MMA lane 0 issued has completed before TMEM is freed
-      if (lane == 0) {
+      if (elect_lane()) {
         tc_commit(drain);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
@@ -367,7 +383,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          const bool w = mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) &&
+          const bool w = mbar_wait(&sf_loaded[stage], phase, abort_flag, p.status, 1u) &&
                          mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u);
           if (!__all_sync(0xffffffffu, w)) {
             ok = false;
@@ -376,14 +392,16 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           tc_fence_after();
           const uint32_t sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
           const uint32_t sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
-          const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
-          const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
-          if (lane == 0) {
+          // atom j of a stage is 512 bytes (32 descriptor address units) after atom 0
+          const uint64_t dsa = desc_sf_atom(smem_u32(smem + L::kSfA + stage * SF::A_SF));
+          const uint64_t dsb = desc_sf_atom(smem_u32(smem + L::kSfB + stage * SF::B_SF));
+          const uint64_t dsb2 = dsb + (SF::B_SF / 2) / 16;
+          if (elect_lane()) {
 #pragma unroll
             for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-              tc_cp_sf(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-              tc_cp_sf(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-              tc_cp_sf(sfb_col + 8 * j + 4, desc_sf_atom(sb + SF::B_SF / 2 + 512 * j));
+              tc_cp_sf(sfa_col + 4 * j, dsa + 32 * j);
+              tc_cp_sf(sfb_col + 8 * j, dsb + 32 * j);
+              tc_cp_sf(sfb_col + 8 * j + 4, dsb2 + 32 * j);
             }
             tc_commit(&sf_full[stage]);
           }
@@ -395,7 +413,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
         }
       }
       // every copy lane 0 issued has completed before TMEM is freed
-      if (lane == 0) {
+      if (elect_lane()) {
         tc_commit(cdrain);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
@@ -484,7 +502,8 @@ struct PairCfg {
   static constexpr uint32_t kBar = kSfB + kStages * kSfb;
   // stage ring, accumulator barriers, drain, scale-factor ring (sf_full,
   // sf_free) and the copier's drain
-  static constexpr uint32_t kNumBars = 4 * kStages + 2 * kNacc + 2;
+  // (+ one more ring: a stage's scale atoms are in shared memory)
+  static constexpr uint32_t kNumBars = 5 * kStages + 2 * kNacc + 2;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
@@ -515,6 +534,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
   uint64_t* sf_full = drain + 1;    // (leader) a stage's scale factors are in both CTAs' TMEM
   uint64_t* sf_free = sf_full + S;  // (leader) the MMAs reading a stage's TMEM slot are done
   uint64_t* cdrain = sf_free + S;
+  uint64_t* sf_loaded = cdrain + 1;  // (leader) both CTAs' scale atoms of a stage have landed
   constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMisc + 4);
@@ -538,6 +558,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&sf_full[s], 1);
       mbar_init(&sf_free[s], 1);
+      mbar_init(&sf_loaded[s], 1);
     }
     mbar_init(cdrain, 1);
     *abort_flag = 0u;
@@ -561,6 +582,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_sh;
   const uint32_t full_leader = mapa_shared(smem_u32(full), 0u);
+  const uint32_t sf_loaded_leader = mapa_shared(smem_u32(sf_loaded), 0u);
   const uint32_t tmem_empty_leader = mapa_shared(smem_u32(tmem_empty), 0u);
 
   if (warp == 0) {
@@ -581,22 +603,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
             ok = false;
             break;
           }
-          // the leader expects both CTAs' bytes on its own barrier
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
+          // The leader expects both CTAs' bytes on its own barriers. The
+          // scale atoms go first, on their own barrier, so the copier moves
+          // them into TMEM while the operand tiles are still in flight; with
+          // one barrier for both, copy latency followed operand latency and
+          // the ring (about 1 us deep for MXFP8) no longer hid the sum.
+          if constexpr (KIND != kPerTensor) {
+            if (rank == 0) mbar_arrive_expect_tx(&sf_loaded[stage], 2 * (C::kSfa + C::kSfb));
+            const uint32_t sb = sf_loaded_leader + 8u * stage;
+            const int kcol = kb * (int)SF::kAtomsK;
+            tma_load_2d_pair(smem + C::kSfA + stage * C::kSfa, &tmap_sfa, 0,
+                             a_atom * (int)p.sf_col_tiles + kcol, sb);
+            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb, &tmap_sfb, 0,
+                             (2 * nb) * (int)p.sf_col_tiles + kcol, sb);
+            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb + C::kSfb / 2, &tmap_sfb, 0,
+                             (2 * nb + 1) * (int)p.sf_col_tiles + kcol, sb);
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
           const uint32_t fb = full_leader + 8u * stage;
           tma_load_2d_pair(smem + C::kA + stage * P_A_BYTES, &tmap_a, kb * BKB,
                            mb * P_BM + 128 * (int)rank, fb);
           tma_load_2d_pair(smem + C::kB + stage * P_B_BYTES, &tmap_b, kb * BKB,
                            nb * P_BN + 128 * (int)rank, fb);
-          if constexpr (KIND != kPerTensor) {
-            const int kcol = kb * (int)SF::kAtomsK;
-            tma_load_2d_pair(smem + C::kSfA + stage * C::kSfa, &tmap_sfa, 0,
-                             a_atom * (int)p.sf_col_tiles + kcol, fb);
-            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb, &tmap_sfb, 0,
-                             (2 * nb) * (int)p.sf_col_tiles + kcol, fb);
-            tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb + C::kSfb / 2, &tmap_sfb, 0,
-                             (2 * nb + 1) * (int)p.sf_col_tiles + kcol, fb);
-          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == S) {
@@ -612,6 +640,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           if (issued & (1u << s)) {
             const uint64_t t0 = globaltimer();
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+            while (KIND != kPerTensor &&
+                   !mbar_try_wait(&sf_loaded[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
           }
@@ -658,8 +690,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           } else if constexpr (KIND != kPerTensor) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&sf_loaded[stage], phase, abort_flag, p.status, 1u))) {
+              ok = false;
+              break;
+            }
           }
-          if (lane == 0) {
+          if (elect_lane()) {
             if constexpr (!kCopier && KIND != kPerTensor) {
               const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
               const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
@@ -697,7 +734,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           }
         }
         if (!ok) break;
-        if (lane == 0) tc_commit_pair(&tmem_full[abuf], 0x3);
+        if (elect_lane()) tc_commit_pair(&tmem_full[abuf], 0x3);
         __syncwarp();
         if (++abuf == C::kNacc) {
           abuf = 0;
@@ -705,7 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
         }
       }
       // every MMA lane 0 issued has completed before the pair frees TMEM
-      if (lane == 0) {
+      if (elect_lane()) {
         tc_commit_pair(drain, 0x1);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
@@ -715,8 +752,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
     }
   } else if (kCopier && warp == 2 + kEpiWarps) {
     // ------------------------------------------------------------ scale-factor copier (leader)
-    // The leader's full barrier counts both CTAs' copies, so once it completes
-    // both CTAs' scale atoms of the stage are in shared memory; each
+    // The leader's sf_loaded barrier counts both CTAs' atom copies, so once it
+    // completes both CTAs' scale atoms of the stage are in shared memory; each
     // tcgen05.cp cta_group::2 moves every CTA's atoms into its own TMEM.
     // The whole warp runs the loop; lane 0 issues the copies and commits.
     if (rank == 0) {
@@ -725,7 +762,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
       bool ok = true;
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          const bool w = mbar_wait(&full[stage], phase, abort_flag, p.status, 1u) &&
+          const bool w = mbar_wait(&sf_loaded[stage], phase, abort_flag, p.status, 1u) &&
                          mbar_wait(&sf_free[stage], phase ^ 1u, abort_flag, p.status, 1u);
           if (!__all_sync(0xffffffffu, w)) {
             ok = false;
@@ -734,14 +771,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           tc_fence_after();
           const uint32_t sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
           const uint32_t sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
-          const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
-          const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
-          if (lane == 0) {
+          // atom j of a stage is 512 bytes (32 descriptor address units) after atom 0
+          const uint64_t dsa = desc_sf_atom(smem_u32(smem + C::kSfA + stage * C::kSfa));
+          const uint64_t dsb = desc_sf_atom(smem_u32(smem + C::kSfB + stage * C::kSfb));
+          const uint64_t dsb2 = dsb + (C::kSfb / 2) / 16;
+          if (elect_lane()) {
 #pragma unroll
             for (uint32_t j = 0; j < SF::kAtomsK; ++j) {
-              tc_cp_sf_pair(sfa_col + 4 * j, desc_sf_atom(sa + 512 * j));
-              tc_cp_sf_pair(sfb_col + 8 * j, desc_sf_atom(sb + 512 * j));
-              tc_cp_sf_pair(sfb_col + 8 * j + 4, desc_sf_atom(sb + C::kSfb / 2 + 512 * j));
+              tc_cp_sf_pair(sfa_col + 4 * j, dsa + 32 * j);
+              tc_cp_sf_pair(sfb_col + 8 * j, dsb + 32 * j);
+              tc_cp_sf_pair(sfb_col + 8 * j + 4, dsb2 + 32 * j);
             }
             tc_commit_pair(&sf_full[stage], 0x1);
           }
@@ -753,7 +792,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
         }
       }
       // every copy lane 0 issued has completed before the pair frees TMEM
-      if (lane == 0) {
+      if (elect_lane()) {
         tc_commit_pair(cdrain, 0x1);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(cdrain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
@@ -939,7 +978,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           const uint32_t alo = desc_sw128_lo(a_base + stage * A_BYTES);
           const uint32_t blo = desc_sw128_lo(b_base + stage * B_BYTES);
           const uint32_t d = tmem + pbuf * kPartialCols;
-          if (lane == 0) {
+          if (elect_lane()) {
 #pragma unroll
             for (uint32_t k = 0; k < 4; ++k)
               mma_f8f6f4(d, dhi | (uint64_t)(alo + 2 * k), dhi | (uint64_t)(blo + 2 * k), idesc,
@@ -956,7 +995,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           if (pbuf == 0) pphase ^= 1u;
         }
       }
-      if (lane == 0) {
+      if (elect_lane()) {
         tc_commit(drain);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(drain, 0u) && globaltimer() - t0 < kWaitLimitNs) {
