@@ -20,6 +20,7 @@ _i64 = ctypes.c_int64
 # name -> argument types (every function returns int status unless noted)
 # brc_cast_ste_block kinds
 STE_BLOCK_FP8, STE_MXFP8, STE_NVFP4, STE_INT4 = 0, 1, 2, 3
+KIND_PERTENSOR_FP8 = 4
 
 PROTOTYPES = {
     "brc_status_string": ([_i], ctypes.c_char_p),
@@ -56,6 +57,9 @@ PROTOTYPES = {
     "brc_gemm_int4": ([_p, _i, _i, _p, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_status": ([_i], _i),
     "brc_selftest_wait_timeout": ([_i, _p, _p], _i),
+    "brc_gemm_bf16": ([_p, _p, _i, _i, _i, _p, _i, _p], _i),
+    "brc_dequant_transposed": ([_p, _i64, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
+    "brc_transpose_u8": ([_p, _i64, _i64, _p, _p], _i),
 }
 
 # status codes (include/breccia_b200.h)

@@ -378,13 +378,17 @@ def _is_scaled(t) -> bool:
     return hasattr(t, "recipe") and hasattr(t, "scale") and hasattr(t, "data")
 
 
-def matmul(a, b, out_dtype=np.float32):
+def matmul(a, b, out_dtype=np.float32, *, b_kmajor=False):
     """Scaled matmul with the reference's semantics (``matmul.py:42-133``):
     ``a (..., M, K) @ b (..., K, N)`` of the dequantized operands with
     float32 accumulation, then ``out_dtype`` (a NumPy dtype as in the
-    reference, or a torch dtype such as ``torch.bfloat16``)."""
+    reference, or a torch dtype such as ``torch.bfloat16``).
+
+    ``b_kmajor`` (extension): ``b`` is an ``(N, K)`` operand cast with its
+    blocks along K (a weight in nn.Linear orientation); the result is
+    ``a @ b^T``, the layout the block-scaled tensor-core GEMMs consume."""
     from . import gemm
-    return gemm.matmul(a, b, _torch_out_dtype(out_dtype))
+    return gemm.matmul(a, b, _torch_out_dtype(out_dtype), b_kmajor=b_kmajor)
 
 
 def linear(a, w, out_dtype=torch.bfloat16):

@@ -9,6 +9,9 @@
 //   kMxfp8     : kind::mxf8f6f4.block_scale, UE8M0 scale per 32 K-elements.
 //   kNvfp4     : kind::mxf4nvf4.block_scale.scale_vec::4X, packed E2M1 codes,
 //                UE4M3 scale per 16 K-elements.
+//   kBf16      : kind::f16 with bf16 operands (64 K-elements per stage), no
+//                scales: the GEMM of dequantized operands for recipe pairs and
+//                orientations without a block-scaled kind.
 // Block scales are consumed in the 512-byte "atom" layout the casts write
 // (128 rows x 4 scale columns per atom).
 //
@@ -44,7 +47,12 @@ namespace gemm {
 
 using namespace sm100;
 
-enum Kind { kPerTensor = 0, kMxfp8 = 1, kNvfp4 = 2 };
+enum Kind { kPerTensor = 0, kMxfp8 = 1, kNvfp4 = 2, kBf16 = 3 };
+// Kinds whose scale factors ride in the MMA (atoms staged and copied to TMEM).
+template <int KIND>
+constexpr bool kScaled = KIND == kMxfp8 || KIND == kNvfp4;
+
+
 
 constexpr int BM = 128;
 constexpr int BN = 256;
@@ -56,8 +64,11 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 // into TMEM (tcgen05.cp), so the copies are issued beside the MMA warp
 // rather than between its MMAs.
 constexpr bool kSfCopier = true;
+// Only block-scaled kinds have the copier warp: the role dispatch gives every
+// warp past the epilogue warps to the copier, so a kind without scale factors
+// must not launch one.
 template <int KIND>
-constexpr int kThreadsG = kThreads + ((kSfCopier && KIND != 0) ? 32 : 0);
+constexpr int kThreadsG = kThreads + ((kSfCopier && kScaled<KIND>) ? 32 : 0);
 constexpr uint32_t A_BYTES = BM * BKB;  // 16 KB
 constexpr uint32_t B_BYTES = BN * BKB;  // 32 KB
 // Tiles are visited in groups of kGroupM row blocks, row block fastest: the
@@ -176,7 +187,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
   uint64_t* sf_free = sf_full + STAGES;  // the MMAs reading a stage's TMEM slot are done
   uint64_t* cdrain = sf_free + STAGES;
   uint64_t* sf_loaded = cdrain + 1;     // a stage's scale atoms are in shared memory
-  constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
+  constexpr bool kCopier = kSfCopier && kScaled<KIND>;
   static_assert(5 * STAGES + 4 <= L::kNumBars, "barrier area too small");
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMisc + 4);
@@ -233,7 +244,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
           // The scale atoms go first and complete on their own barrier, so
           // their copies into TMEM can run while the operand tiles are
           // still in flight instead of after them.
-          if constexpr (KIND != kPerTensor) {
+          if constexpr (kScaled<KIND>) {
             const bool b_hi = (2 * nb + 1) < p.sfb_row_atoms;
             const uint32_t kcol = (uint32_t)kb * SF::kAtomsK;
             mbar_arrive_expect_tx(&sf_loaded[stage], SF::A_SF + (b_hi ? SF::B_SF : SF::B_SF / 2));
@@ -267,7 +278,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
-            while (KIND != kPerTensor &&
+            while (kScaled<KIND> &&
                    !mbar_try_wait(&sf_loaded[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
@@ -311,7 +322,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
               break;
             }
             tc_fence_after();
-          } else if constexpr (KIND != kPerTensor) {
+          } else if constexpr (kScaled<KIND>) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + STAGES * SF::SFA_COLS + stage * SF::SFB_COLS;
             if (!__all_sync(0xffffffffu,
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
             }
           }
           if (elect_lane()) {
-            if constexpr (!kCopier && KIND != kPerTensor) {
+            if constexpr (!kCopier && kScaled<KIND>) {
               const uint32_t sa = smem_u32(smem + L::kSfA + stage * SF::A_SF);
               const uint32_t sb = smem_u32(smem + L::kSfB + stage * SF::B_SF);
 #pragma unroll
@@ -338,6 +349,8 @@ __global__ void __launch_bounds__(kThreadsG<KIND>, 1)
               const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
               if constexpr (KIND == kPerTensor) {
                 mma_f8f6f4(tmem + ACC_COL, ad, bd, idesc_f8f6f4(AFMT, BFMT, BM, BN), acc);
+              } else if constexpr (KIND == kBf16) {
+                mma_bf16(tmem + ACC_COL, ad, bd, idesc_bf16(BM, BN), acc);
               } else if constexpr (KIND == kMxfp8) {
                 mma_mxf8f6f4(tmem + ACC_COL, ad, bd,
                              idesc_block_scaled(AFMT, BFMT, BM, BN, 1u, k, k),
@@ -493,8 +506,8 @@ struct PairCfg {
   static constexpr uint32_t kSfa = SF::A_SF;  // scale atoms of this CTA's 128 A rows
   static constexpr uint32_t kSfb = SF::B_SF;  // scale atoms of the tile's 256 B^T rows
   static constexpr uint32_t kStageBytes = P_A_BYTES + P_B_BYTES + kSfa + kSfb;
-  static constexpr int kNacc = KIND == kPerTensor ? 2 : 1;  // accumulator buffers
-  static constexpr int kStages = KIND == kPerTensor ? 7 : (KIND == kMxfp8 ? 6 : 5);
+  static constexpr int kNacc = kScaled<KIND> ? 1 : 2;  // accumulator buffers
+  static constexpr int kStages = kScaled<KIND> ? (KIND == kMxfp8 ? 6 : 5) : 7;
   static constexpr uint32_t kA = 0;
   static constexpr uint32_t kB = kA + kStages * P_A_BYTES;
   static constexpr uint32_t kSfA = kB + kStages * P_B_BYTES;
@@ -508,8 +521,8 @@ struct PairCfg {
   static constexpr uint32_t kTotal = kMisc + 16;
   static constexpr uint32_t kAlloc = kTotal + 1024;  // manual 1024-byte alignment
   static_assert(kAlloc <= 227 * 1024, "pair ring exceeds shared memory");
-  static_assert(kNacc * 256 + (KIND == kPerTensor ? 0
-                                                  : kStages * (SF::SFA_COLS + SF::SFB_COLS)) <=
+  static_assert(kNacc * 256 + (!kScaled<KIND> ? 0
+                                              : kStages * (SF::SFA_COLS + SF::SFB_COLS)) <=
                     TMEM_COLS,
                 "TMEM overflow");
 };
@@ -535,7 +548,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
   uint64_t* sf_free = sf_full + S;  // (leader) the MMAs reading a stage's TMEM slot are done
   uint64_t* cdrain = sf_free + S;
   uint64_t* sf_loaded = cdrain + 1;  // (leader) both CTAs' scale atoms of a stage have landed
-  constexpr bool kCopier = kSfCopier && KIND != kPerTensor;
+  constexpr bool kCopier = kSfCopier && kScaled<KIND>;
   uint32_t* tmem_base_sh = reinterpret_cast<uint32_t*>(smem + C::kMisc);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kMisc + 4);
 
@@ -567,7 +580,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
-    if constexpr (KIND != kPerTensor) {
+    if constexpr (kScaled<KIND>) {
       prefetch_tmap(&tmap_sfa);
       prefetch_tmap(&tmap_sfb);
     }
@@ -608,7 +621,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
           // them into TMEM while the operand tiles are still in flight; with
           // one barrier for both, copy latency followed operand latency and
           // the ring (about 1 us deep for MXFP8) no longer hid the sum.
-          if constexpr (KIND != kPerTensor) {
+          if constexpr (kScaled<KIND>) {
             if (rank == 0) mbar_arrive_expect_tx(&sf_loaded[stage], 2 * (C::kSfa + C::kSfb));
             const uint32_t sb = sf_loaded_leader + 8u * stage;
             const int kcol = kb * (int)SF::kAtomsK;
@@ -642,7 +655,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
-            while (KIND != kPerTensor &&
+            while (kScaled<KIND> &&
                    !mbar_try_wait(&sf_loaded[s], (issued_parity >> s) & 1u) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
@@ -687,7 +700,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
               break;
             }
             tc_fence_after();
-          } else if constexpr (KIND != kPerTensor) {
+          } else if constexpr (kScaled<KIND>) {
             sfa_col = tmem + SF_COL + stage * SF::SFA_COLS;
             sfb_col = tmem + SF_COL + S * SF::SFA_COLS + stage * SF::SFB_COLS;
             if (!__all_sync(0xffffffffu,
@@ -697,7 +710,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
             }
           }
           if (elect_lane()) {
-            if constexpr (!kCopier && KIND != kPerTensor) {
+            if constexpr (!kCopier && kScaled<KIND>) {
               const uint32_t sa = smem_u32(smem + C::kSfA + stage * C::kSfa);
               const uint32_t sb = smem_u32(smem + C::kSfB + stage * C::kSfb);
 #pragma unroll
@@ -714,6 +727,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
               const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
               if constexpr (KIND == kPerTensor) {
                 mma_f8f6f4_pair(dacc, ad, bd, idesc_f8f6f4(AFMT, BFMT, P_BM, P_BN), acc);
+              } else if constexpr (KIND == kBf16) {
+                mma_bf16_pair(dacc, ad, bd, idesc_bf16(P_BM, P_BN), acc);
               } else if constexpr (KIND == kMxfp8) {
                 mma_mxf8f6f4_pair(dacc, ad, bd,
                                   idesc_block_scaled(AFMT, BFMT, P_BM, P_BN, 1u, k, k),
@@ -1506,6 +1521,35 @@ int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, 
   if (a_fmt == BRC_FP8_E4M3) return launch_block_out<0, 1>(d_dtype, ta, tb, p, st);
   if (b_fmt == BRC_FP8_E4M3) return launch_block_out<1, 0>(d_dtype, ta, tb, p, st);
   return launch_block_out<1, 1>(d_dtype, ta, tb, p, st);
+}
+
+int brc_gemm_bf16(const void* a, const void* b, int M, int N, int K, void* d, int d_dtype,
+                  void* stream) {
+  int rc = check_common(a, b, d, M, N, K, d_dtype, 8);
+  if (rc) return rc;
+  if ((int64_t)M * N == 0) return BRC_OK;
+  if (K == 0) return BRC_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint64_t row_bytes = 2ull * (uint64_t)K;
+  // 64 bf16 (128 bytes) of K per stage; a partial last stage reads zeros
+  // past the row end (the tensor map's out-of-bounds fill), adding nothing.
+  const int num_kb = (int)((row_bytes + BKB - 1) / BKB);
+  CUtensorMap ta, tb;
+  if (use_pairs(M, N)) {
+    if ((rc = make_tmap(&ta, a, M, row_bytes, 128))) return rc;
+    if ((rc = make_tmap(&tb, b, N, row_bytes, 128))) return rc;
+    Params p = base_params(M, N, K, 64, d);
+    p.num_kb = num_kb;
+    to_pair_params(p);
+    p.status = status_word();
+    return launch_pair_out<kBf16, 0, 0>(d_dtype, ta, tb, ta, tb, p, st);
+  }
+  if ((rc = make_tmap(&ta, a, M, row_bytes, BM))) return rc;
+  if ((rc = make_tmap(&tb, b, N, row_bytes, BN))) return rc;
+  Params p = base_params(M, N, K, 64, d);
+  p.num_kb = num_kb;
+  p.status = status_word();
+  return launch_out<kBf16, 0, 0>(d_dtype, ta, tb, p, st);
 }
 
 int brc_selftest_wait_timeout(int limit_us, int* roles_out, void* stream) {

@@ -1,0 +1,270 @@
+// Layout kernels for breccia's own matmul orientation.
+//
+// breccia's matmul(a, b) takes b as (K, N) with its scale blocks along the
+// last axis, N (src/breccia/kernels/reference/matmul.py:123-133 multiplies the
+// dequantized operands; cast.py blocks the last axis). The tensor-core GEMMs
+// consume both operands K-major, (rows, K). These kernels move a (K, N)
+// operand into the (N, K) orientation on the way:
+//
+//   k_dequant_t    decode(code) * scale of a block-scaled (rows, cols) tensor
+//                  (any recipe: per-tensor FP8, block FP8, MXFP8, NVFP4, INT4),
+//                  written transposed as (cols, rows) float32 / bf16 / f16.
+//                  The products are the reference's float32 dequantize
+//                  (cast.py:376-586), then rounded once to the output type.
+//   k_transpose_u8 (rows, cols) bytes -> (cols, rows): per-tensor FP8 codes do
+//                  not depend on orientation, so they move as plain bytes.
+//
+// Both stage 64 x 64 tiles through shared memory: every thread loads 16
+// consecutive elements of one source row (16-byte loads) and stores 16
+// consecutive elements of one destination row, so global traffic stays
+// coalesced in both orientations.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "breccia_b200.h"
+#include "common.cuh"
+#include "launch.h"
+
+namespace brc {
+namespace {
+
+constexpr int kTile = 64;
+constexpr int kThreads = 256;
+
+struct DqtArgs {
+  const uint8_t* codes;
+  const void* scales;
+  const void* zp;
+  void* out;
+  int64_t rows, cols;
+  int block;           // scale run along cols
+  int64_t scale_cols;  // cols / block
+  int is_signed;
+  int scale_f16;
+};
+
+int grid_tiles(int64_t tiles) {
+  const int64_t cap = (int64_t)sm_count() * 8;
+  return (int)(tiles < cap ? (tiles < 1 ? 1 : tiles) : cap);
+}
+
+__device__ __forceinline__ float e8m0_value(uint32_t e) {
+  // 2^(e - 127) in float32, as the reference's float32 power gives it:
+  // e = 0 is the subnormal 2^-127, e = 255 overflows to +inf.
+  if (e == 255u) return __uint_as_float(0x7F800000u);
+  if (e == 0u) return __uint_as_float(0x00400000u);
+  return __uint_as_float(e << 23);
+}
+
+template <int OUT>
+__device__ __forceinline__ void store8(void* out, int64_t e0, const float* v) {
+  if constexpr (OUT == BRC_DTYPE_F32) {
+    float* o = static_cast<float*>(out) + e0;
+    stg16(o, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                        __float_as_uint(v[3])));
+    stg16(o + 4, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]),
+                            __float_as_uint(v[6]), __float_as_uint(v[7])));
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (OUT == BRC_DTYPE_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    stg16(static_cast<char*>(out) + e0 * 2, make_uint4(w[0], w[1], w[2], w[3]));
+  }
+}
+
+// KIND: BRC_STE_BLOCK_FP8, BRC_STE_MXFP8, BRC_STE_NVFP4, BRC_STE_INT4 or
+// BRC_KIND_PERTENSOR_FP8. rows % 8 == 0, cols % 16 == 0, block % 16 == 0.
+template <int KIND, int FMT, int OUT>
+__global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
+  __shared__ float tile[kTile][kTile + 1];
+  const int64_t tiles_r = (a.rows + kTile - 1) / kTile;
+  const int64_t tiles_c = (a.cols + kTile - 1) / kTile;
+  const int lr = threadIdx.x >> 2;          // tile row this thread loads / column it stores
+  const int lc = (threadIdx.x & 3) * 16;    // 16-element segment
+  for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
+    const int64_t r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
+    const int64_t r = r0 + lr, c = c0 + lc;
+    float v[16];
+    if (r < a.rows && c < a.cols) {
+      const uint4 cv = ldg16(a.codes + r * a.cols + c);
+      const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
+      float scale = 0.f, zp = 0.f;
+      if constexpr (KIND == BRC_KIND_PERTENSOR_FP8) {
+        scale = *static_cast<const float*>(a.scales);
+      } else {
+        const int64_t si = r * a.scale_cols + c / a.block;
+        if constexpr (KIND == BRC_STE_BLOCK_FP8) {
+          scale = static_cast<const float*>(a.scales)[si];
+        } else if constexpr (KIND == BRC_STE_MXFP8) {
+          scale = e8m0_value(static_cast<const uint8_t*>(a.scales)[si]);
+        } else if constexpr (KIND == BRC_STE_NVFP4) {
+          scale = dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
+        } else {
+          if (a.scale_f16) {
+            scale = __half2float(static_cast<const __half*>(a.scales)[si]);
+            if (a.zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
+          } else {
+            scale = static_cast<const float*>(a.scales)[si];
+            if (a.zp) zp = static_cast<const float*>(a.zp)[si];
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t code = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        float d;
+        if constexpr (KIND == BRC_STE_NVFP4) {
+          d = dec_e2m1(code);
+        } else if constexpr (KIND == BRC_STE_INT4) {
+          const uint32_t lo = code & 0xFu;
+          d = (a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+          if (a.zp) d = __fsub_rn(d, zp);
+        } else {
+          d = dec_fp8<FMT>(code);
+        }
+        v[i] = __fmul_rn(d, scale);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    }
+    __syncthreads();  // the previous tile's readers are done with `tile`
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tile[lc + i][lr] = v[i];
+    __syncthreads();
+    const int64_t oc = c0 + lr;  // destination row (a source column)
+    if (oc < a.cols) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t orow = r0 + lc + 8 * h;  // first source row of these 8
+        if (orow < a.rows) {
+          float w8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w8[i] = tile[lr][lc + 8 * h + i];
+          store8<OUT>(a.out, oc * a.rows + orow, w8);
+        }
+      }
+    }
+  }
+}
+
+// (rows, cols) bytes -> (cols, rows); rows % 16 == 0, cols % 16 == 0.
+__global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __restrict__ in,
+                                                          int64_t rows, int64_t cols,
+                                                          uint8_t* __restrict__ out) {
+  __shared__ uint8_t tile[kTile][kTile + 4];
+  const int64_t tiles_r = (rows + kTile - 1) / kTile;
+  const int64_t tiles_c = (cols + kTile - 1) / kTile;
+  const int lr = threadIdx.x >> 2, lc = (threadIdx.x & 3) * 16;
+  for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
+    const int64_t r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
+    const int64_t r = r0 + lr, c = c0 + lc;
+    uint4 cv = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows && c < cols) cv = ldg16(in + r * cols + c);
+    const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tile[lc + i][lr] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+    __syncthreads();
+    const int64_t oc = c0 + lr, orow = r0 + lc;
+    if (oc < cols && orow < rows) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = (uint32_t)tile[lr][lc + 4 * j] | ((uint32_t)tile[lr][lc + 4 * j + 1] << 8) |
+               ((uint32_t)tile[lr][lc + 4 * j + 2] << 16) |
+               ((uint32_t)tile[lr][lc + 4 * j + 3] << 24);
+      stg16(out + oc * rows + orow, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+template <int KIND, int FMT>
+int launch_dqt(const DqtArgs& a, int out_dtype, cudaStream_t st) {
+  const int64_t tiles = ((a.rows + kTile - 1) / kTile) * ((a.cols + kTile - 1) / kTile);
+  const int grid = grid_tiles(tiles);
+  if (out_dtype == BRC_DTYPE_F32)
+    k_dequant_t<KIND, FMT, BRC_DTYPE_F32><<<grid, kThreads, 0, st>>>(a);
+  else if (out_dtype == BRC_DTYPE_BF16)
+    k_dequant_t<KIND, FMT, BRC_DTYPE_BF16><<<grid, kThreads, 0, st>>>(a);
+  else
+    k_dequant_t<KIND, FMT, BRC_DTYPE_F16><<<grid, kThreads, 0, st>>>(a);
+  return check_launch();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace brc
+
+using namespace brc;
+
+extern "C" {
+
+int brc_dequant_transposed(const uint8_t* codes, int64_t rows, int64_t cols, int kind, int fmt,
+                           int block, int is_signed, int scale_dtype, const void* scales,
+                           const void* zero_points, void* out, int out_dtype, void* stream) {
+  if (rows < 0 || cols < 0) return BRC_ERR_SHAPE;
+  if ((!codes || !scales || !out) && rows * cols > 0) return BRC_ERR_NULL;
+  if (out_dtype != BRC_DTYPE_F32 && out_dtype != BRC_DTYPE_BF16 && out_dtype != BRC_DTYPE_F16)
+    return BRC_ERR_DTYPE;
+  if (fmt != BRC_FP8_E4M3 && fmt != BRC_FP8_E5M2) return BRC_ERR_DTYPE;
+  if (kind == BRC_STE_MXFP8) block = 32;
+  if (kind == BRC_STE_NVFP4) block = 16;
+  if (kind == BRC_KIND_PERTENSOR_FP8) block = 16;
+  if (kind < 0 || kind > BRC_KIND_PERTENSOR_FP8) return BRC_ERR_UNSUPPORTED;
+  if (block <= 0 || block % 16 || cols % block || cols % 16 || rows % 8) return BRC_ERR_SHAPE;
+  if (kind == BRC_STE_INT4 && scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32)
+    return BRC_ERR_DTYPE;
+  if (rows * cols == 0) return BRC_OK;
+  if (!aligned16(codes) || !aligned16(out)) return BRC_ERR_ALIGN;
+  DqtArgs a{};
+  a.codes = codes;
+  a.scales = scales;
+  a.zp = zero_points;
+  a.out = out;
+  a.rows = rows;
+  a.cols = cols;
+  a.block = block;
+  a.scale_cols = cols / block;
+  a.is_signed = is_signed ? 1 : 0;
+  a.scale_f16 = scale_dtype == BRC_SCALE_F16;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool e4 = fmt == BRC_FP8_E4M3;
+  switch (kind) {
+    case BRC_STE_BLOCK_FP8:
+      return e4 ? launch_dqt<BRC_STE_BLOCK_FP8, BRC_FP8_E4M3>(a, out_dtype, st)
+                : launch_dqt<BRC_STE_BLOCK_FP8, BRC_FP8_E5M2>(a, out_dtype, st);
+    case BRC_STE_MXFP8:
+      return e4 ? launch_dqt<BRC_STE_MXFP8, BRC_FP8_E4M3>(a, out_dtype, st)
+                : launch_dqt<BRC_STE_MXFP8, BRC_FP8_E5M2>(a, out_dtype, st);
+    case BRC_STE_NVFP4:
+      return launch_dqt<BRC_STE_NVFP4, BRC_FP8_E4M3>(a, out_dtype, st);
+    case BRC_STE_INT4:
+      return launch_dqt<BRC_STE_INT4, BRC_FP8_E4M3>(a, out_dtype, st);
+    default:
+      return e4 ? launch_dqt<BRC_KIND_PERTENSOR_FP8, BRC_FP8_E4M3>(a, out_dtype, st)
+                : launch_dqt<BRC_KIND_PERTENSOR_FP8, BRC_FP8_E5M2>(a, out_dtype, st);
+  }
+}
+
+int brc_transpose_u8(const uint8_t* in, int64_t rows, int64_t cols, uint8_t* out, void* stream) {
+  if (rows < 0 || cols < 0 || rows % 16 || cols % 16) return BRC_ERR_SHAPE;
+  if ((!in || !out) && rows * cols > 0) return BRC_ERR_NULL;
+  if (rows * cols == 0) return BRC_OK;
+  if (!aligned16(in) || !aligned16(out)) return BRC_ERR_ALIGN;
+  const int64_t tiles = ((rows + kTile - 1) / kTile) * ((cols + kTile - 1) / kTile);
+  k_transpose_u8<<<grid_tiles(tiles), kThreads, 0, (cudaStream_t)stream>>>(in, rows, cols, out);
+  return check_launch();
+}
+
+}  // extern "C"

@@ -182,6 +182,16 @@ __device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, FP32 accumulate (kind::f16).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Block-scaled MXFP8: scale factors (UE8M0) read from TMEM.
 __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                              uint32_t idesc, uint32_t sfa_tmem,
@@ -321,6 +331,11 @@ __host__ __device__ constexpr uint32_t idesc_f8f6f4(uint32_t afmt, uint32_t bfmt
                                                     uint32_t n) {
   return (1u << 4) | (afmt << 7) | (bfmt << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+// Instruction descriptor, kind::f16 with bf16 A and B (format code 1 in both
+// fields), F32 accumulator, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
 // Instruction descriptor, block-scaled kinds: B scale-factor byte id in
 // [4,6), A/B formats in [7,10) / [10,13), N >> 3 in [17,23), scale format in
 // bit 23 (0 = UE4M3, 1 = UE8M0), M >> 4 in [24,29), A scale-factor byte id in
@@ -418,6 +433,15 @@ __device__ __forceinline__ void mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t ades
       "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::
           "r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void mma_mxf4nvf4_4x_pair(uint32_t d_tmem, uint64_t adesc,

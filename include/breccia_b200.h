@@ -213,6 +213,7 @@ int brc_int4_tiles(const uint8_t* codes, int64_t rows, int64_t cols, const void*
 #define BRC_STE_MXFP8 1
 #define BRC_STE_NVFP4 2
 #define BRC_STE_INT4 3
+#define BRC_KIND_PERTENSOR_FP8 4
 int brc_cast_ste_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt,
                                uint32_t* amax_word, float* out, void* stream);
 int brc_cast_ste_block(const void* x, int x_dtype, int64_t rows, int64_t cols, int kind,
@@ -295,6 +296,38 @@ int brc_gemm_block_fp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, 
 int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_tiles, int N, int is_signed,
                   int symmetric, const float* scale_tiles, const float* zp_tiles, void* d,
                   int d_dtype, void* stream);
+/* Dense bf16 GEMM on the tensor cores (tcgen05 kind::f16, float32 accumulate):
+ * d[M, N] = a[M, K] * b[N, K]^T, both bf16 and K-major, K % 8 == 0 (a partial
+ * last 64-element K step reads zeros), N % 16 == 0, 16-byte aligned.
+ * This is the reference's matmul for operand pairs without a block-scaled
+ * tensor-core kind: matmul.py:123-133 dequantizes both operands to float32
+ * and multiplies. Operands that dequantize exactly into bf16 (MXFP8:
+ * E4M3/E5M2 x 2^k; NVFP4: E2M1 x E4M3, at most 6 significant bits) give the
+ * reference's products exactly, with float32 accumulation; block FP8,
+ * per-tensor FP8 and INT4 values are rounded once to bf16 (relative error
+ * <= 2^-9 per element). */
+int brc_gemm_bf16(const void* a, const void* b, int M, int N, int K, void* d, int d_dtype,
+                  void* stream);
+
+/* ======================================================= layout
+ * breccia's matmul takes b as (K, N) with scale blocks along N
+ * (src/breccia/kernels/reference/matmul.py:123-133; cast.py blocks the last
+ * axis); the tensor-core GEMMs take operands K-major (N, K). */
+/* decode(code) * scale of a (rows, cols) tensor, written transposed as
+ * (cols, rows) in out_dtype (float32 / bf16 / f16): the reference's float32
+ * dequantize (cast.py:376-586) rounded once to the output type. kind:
+ * BRC_STE_BLOCK_FP8 (float32 scales (rows, cols / block)), BRC_STE_MXFP8
+ * (E8M0 bytes, block 32), BRC_STE_NVFP4 (E4M3 bytes, block 16; fmt ignored),
+ * BRC_STE_INT4 (scale_dtype BRC_SCALE_F16 / F32, zero_points optional, block
+ * = group, is_signed), BRC_KIND_PERTENSOR_FP8 (scales -> one float32).
+ * rows % 8 == 0, cols % 16 == 0, block % 16 == 0. */
+int brc_dequant_transposed(const uint8_t* codes, int64_t rows, int64_t cols, int kind, int fmt,
+                           int block, int is_signed, int scale_dtype, const void* scales,
+                           const void* zero_points, void* out, int out_dtype, void* stream);
+/* (rows, cols) bytes -> (cols, rows), rows % 16 == 0, cols % 16 == 0: per-tensor
+ * FP8 codes in breccia's (K, N) orientation into the GEMM's (N, K). */
+int brc_transpose_u8(const uint8_t* in, int64_t rows, int64_t cols, uint8_t* out, void* stream);
+
 /* Sticky device status of the GEMM kernels on the current device (bit 0: a
  * bounded wait timed out and the kernel returned early). Synchronous. The
  * status word's address is looked up once per device and kept for the life
