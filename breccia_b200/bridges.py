@@ -39,7 +39,8 @@ from . import _lib
 from . import types as T
 from .api import _aligned, _remember, _stream, attach_gemm_operands
 
-__all__ = ["save_safetensors", "load_safetensors"]
+__all__ = ["save_safetensors", "load_safetensors", "to_transformer_engine",
+           "from_transformer_engine"]
 
 _PACKED_FORMAT = "breccia_nibbles_high_first"
 _FOUR_BIT = ("nvfp4", "int4")
@@ -214,3 +215,91 @@ def load_safetensors(path: str, *, device: Any = None) -> Dict[str, Any]:
                 attach_gemm_operands(st)
             out[name] = st
     return out
+
+
+# ------------------------------------------------------------ TransformerEngine
+# Reference: src/breccia/bridges/_transformer_engine.py:63-196. A TE
+# Float8Tensor carries `_data` (uint8 FP8 bytes), `_scale_inv` (float32 of
+# shape (1,), the dequantization scale -- breccia's ScaledTensor.scale) and
+# `_fp8_dtype`. The per-tensor GPU outputs of this backend already have that
+# form, so both directions share the buffers: no copy, no kernel. TE rounds
+# ties to even in its own casts; codes made here round ties toward zero, as
+# breccia's NumPy path does (the values they decode to are the same ones).
+
+_TE_MODULES = ("transformer_engine.pytorch.tensor.float8_tensor",
+               "transformer_engine.pytorch.tensor", "transformer_engine.pytorch.float8_tensor",
+               "transformer_engine.pytorch")
+_TE_DTYPE_MODULES = ("transformer_engine_torch", "transformer_engine.pytorch.cpp_extensions",
+                     "transformer_engine.pytorch.tensor.float8_tensor", "transformer_engine.pytorch",
+                     "transformer_engine.common.recipe")
+
+
+def _te_attr(modules, attr):
+    import importlib
+    for name in modules:
+        try:
+            mod = importlib.import_module(name)
+        except ImportError:
+            continue
+        if hasattr(mod, attr):
+            return getattr(mod, attr)
+    return None
+
+
+def _require_te():
+    try:
+        import transformer_engine.pytorch  # noqa: F401
+    except ImportError as e:  # the reference's message (_transformer_engine.py:41-52)
+        raise ImportError("TransformerEngine is required for the TE bridge. Install with: "
+                          "pip install transformer-engine (Linux + CUDA only)") from e
+
+
+def to_transformer_engine(scaled):
+    """Per-tensor FP8 ScaledTensor on the GPU -> TE ``Float8Tensor`` sharing
+    its buffers (``_transformer_engine.py:91-196``): ``data`` viewed as
+    uint8, the 0-d float32 scale viewed as shape (1,)."""
+    _require_te()
+    if getattr(scaled.recipe, "name", None) not in ("delayed", "current"):
+        raise NotImplementedError(
+            "to_transformer_engine supports DelayedScaling / Float8CurrentScaling only, got "
+            f"{type(scaled.recipe).__name__}")
+    data = scaled.data
+    if not isinstance(data, torch.Tensor) or not data.is_cuda:
+        raise TypeError("to_transformer_engine here takes CUDA tensors")
+    if data.element_size() != 1:
+        raise ValueError("to_transformer_engine requires 1-byte data dtype (uint8 or "
+                         f"torch.float8_*), got {data.dtype}")
+    Float8Tensor = _te_attr(_TE_MODULES, "Float8Tensor")
+    DType = _te_attr(_TE_DTYPE_MODULES, "DType")
+    if Float8Tensor is None or DType is None:
+        raise RuntimeError("Could not locate TransformerEngine's Float8Tensor / DType")
+    scale_inv = scaled.scale
+    if scale_inv.dtype != torch.float32:
+        scale_inv = scale_inv.to(torch.float32)
+    fp8 = DType.kFloat8E4M3 if scaled.recipe.fp8_format == "E4M3" else DType.kFloat8E5M2
+    return Float8Tensor(data=data.view(torch.uint8), fp8_scale_inv=scale_inv.reshape(1),
+                        fp8_dtype=fp8)
+
+
+def from_transformer_engine(te_tensor, recipe=None):
+    """TE ``Float8Tensor`` -> ScaledTensor sharing ``_data`` and
+    ``_scale_inv`` (``_transformer_engine.py:63-88``): the (1,)-shaped scale
+    viewed as 0-d, recipe ``DelayedScaling`` with the TE dtype's format
+    unless given."""
+    _require_te()
+    data = te_tensor._data
+    scale = te_tensor._scale_inv
+    if hasattr(scale, "squeeze") and scale.ndim == 1 and scale.shape[0] == 1:
+        scale = scale.squeeze(0)
+    if recipe is None:
+        name = repr(getattr(te_tensor, "_fp8_dtype", "E4M3")).lower()
+        if "e4m3" in name:
+            fmt = "E4M3"
+        elif "e5m2" in name:
+            fmt = "E5M2"
+        else:
+            raise ValueError(f"unknown TE FP8 dtype: {te_tensor._fp8_dtype!r}")
+        recipe = T.DelayedScaling(fp8_format=fmt)
+    from .api import _classes
+    ST, L = _classes(recipe)
+    return ST(data=data, scale=scale, recipe=recipe, layout=L.PerTensor())

@@ -218,3 +218,71 @@ def test_dlpack_zero_copy_of_outputs():
             assert back.data_ptr() == t.data_ptr() and back.dtype == t.dtype
         u8 = torch.from_dlpack(st.data.view(torch.uint8))
         assert u8.data_ptr() == st.data.data_ptr()
+
+
+# ------------------------------------------------------------ TransformerEngine
+# TE is not installed in this image; a module with TE's Float8Tensor
+# constructor and DType enum (the attribute shape the reference's own
+# validation uses, benchmarks/modal_te_validate.py:130-174) stands in for it.
+
+@pytest.fixture
+def fake_te(monkeypatch):
+    import enum
+    import sys
+    import types as pytypes
+
+    class DType(enum.Enum):
+        kFloat8E4M3 = 7
+        kFloat8E5M2 = 8
+
+    class Float8Tensor:
+        def __init__(self, *, data, fp8_scale_inv, fp8_dtype):
+            self._data, self._scale_inv, self._fp8_dtype = data, fp8_scale_inv, fp8_dtype
+
+        def dequantize(self):
+            fdt = torch.float8_e4m3fn if self._fp8_dtype == DType.kFloat8E4M3 else torch.float8_e5m2
+            return self._data.view(fdt).to(torch.float32) * self._scale_inv
+
+    te = pytypes.ModuleType("transformer_engine")
+    te_pt = pytypes.ModuleType("transformer_engine.pytorch")
+    te_pt.Float8Tensor = Float8Tensor
+    te_torch = pytypes.ModuleType("transformer_engine_torch")
+    te_torch.DType = DType
+    te.pytorch = te_pt
+    for name, mod in (("transformer_engine", te), ("transformer_engine.pytorch", te_pt),
+                      ("transformer_engine_torch", te_torch)):
+        monkeypatch.setitem(sys.modules, name, mod)
+    return Float8Tensor, DType
+
+
+@pytest.mark.parametrize("fmt", ["E4M3", "E5M2"])
+def test_transformer_engine_round_trip_shares_buffers(fake_te, fmt):
+    """GPU per-tensor output -> Float8Tensor -> ScaledTensor: the same device
+    buffers throughout, TE's dequantize equals this backend's bit for bit."""
+    import breccia_b200 as bb
+    from breccia_b200 import bridges
+    Float8Tensor, DType = fake_te
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(256, 512, generator=g) * 3).cuda()
+    st = bb.cast(x, bb.Float8CurrentScaling(fp8_format=fmt))
+    te_t = bridges.to_transformer_engine(st)
+    assert isinstance(te_t, Float8Tensor)
+    assert te_t._fp8_dtype == (DType.kFloat8E4M3 if fmt == "E4M3" else DType.kFloat8E5M2)
+    assert te_t._data.dtype == torch.uint8 and tuple(te_t._scale_inv.shape) == (1,)
+    assert te_t._data.data_ptr() == st.data.data_ptr()
+    assert te_t._scale_inv.data_ptr() == st.scale.data_ptr()
+    assert torch.equal(te_t.dequantize().view(torch.int32), bb.dequantize(st).view(torch.int32))
+    back = bridges.from_transformer_engine(te_t)
+    assert back.recipe.name == "delayed" and back.recipe.fp8_format == fmt
+    assert back.scale.ndim == 0 and back.data.data_ptr() == st.data.data_ptr()
+    assert torch.equal(bb.dequantize(back), bb.dequantize(st))
+    with pytest.raises(NotImplementedError):
+        bridges.to_transformer_engine(bb.cast(x, bb.MXFP8BlockScaling()))
+
+
+def test_transformer_engine_missing_raises():
+    from breccia_b200 import bridges
+    import breccia_b200 as bb
+    st = bb.cast(torch.randn(16, 32).cuda(), bb.Float8CurrentScaling())
+    with pytest.raises(ImportError, match="TransformerEngine is required"):
+        bridges.to_transformer_engine(st)
