@@ -875,15 +875,168 @@ __device__ __forceinline__ void store_out16(void* out, int64_t e0, const float* 
   }
 }
 
+// FP8 pairs to f16 pairs by the hardware conversion: every E4M3 / E5M2 value
+// (subnormals, infinities and NaN included) is exact in float16 and again in
+// float32, so the float32 product below rounds exactly once, as the
+// reference's decode-then-multiply does. Byte i of the pair lands in half i.
+template <int FMT>
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint16_t b = (uint16_t)two;
+  if constexpr (FMT == BRC_FP8_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(b));
+  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(b));
+  return d;
+}
+// Two E2M1 codes (one per byte, low nibbles) to f16 pairs, exactly.
+__device__ __forceinline__ uint32_t e2m1_bytes_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint32_t pair = (two & 0x0Fu) | ((two >> 4) & 0xF0u);
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(d)
+      : "r"(pair));
+  return d;
+}
+__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
+  const __half2 v = *reinterpret_cast<const __half2*>(&h);
+  lo = __low2float(v);
+  hi = __high2float(v);
+}
+
+__device__ __forceinline__ uint32_t ldg4(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void stg8(void* p, uint32_t a, uint32_t b) {
+  asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+
+// 16 codes (one 16-byte word group) -> 16 decoded float32 values.
+template <int DQ, int FMT>
+__device__ __forceinline__ void decode4(uint32_t w, float (&v)[4], int is_signed, bool has_zp,
+                                        float zp) {
+  if constexpr (DQ == kDqFp8 || DQ == kDqMx) {
+    f16x2_to_f32(fp8x2_to_f16x2<FMT>(w), v[0], v[1]);
+    f16x2_to_f32(fp8x2_to_f16x2<FMT>(w >> 16), v[2], v[3]);
+  } else if constexpr (DQ == kDqNv) {
+    f16x2_to_f32(e2m1_bytes_to_f16x2(w), v[0], v[1]);
+    f16x2_to_f32(e2m1_bytes_to_f16x2(w >> 16), v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = (w >> (8 * i)) & 0xFu;
+      float d = (is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+      if (has_zp) d = __fsub_rn(d, zp);
+      v[i] = d;
+    }
+  }
+}
+template <int DQ, int FMT>
+__device__ __forceinline__ void decode16(const uint32_t (&w)[4], float (&v)[16], int is_signed,
+                                         bool has_zp, float zp) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float q[4];
+    decode4<DQ, FMT>(w[j], q, is_signed, has_zp, zp);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[4 * j + i] = q[i];
+  }
+}
+
+// Scale (and zero point) of the 16-code chunk `c`.
+template <int DQ>
+__device__ __forceinline__ float chunk_scale(const DequantArgs& a, uint32_t c, const FastDiv& cpr,
+                                             const FastDiv& bm, const FastDiv& cpb, float& zp,
+                                             bool& has_zp) {
+  const uint32_t row = fdiv(c, cpr);
+  const uint32_t cin = c - row * cpr.d;  // chunk within the row
+  const int64_t si = (int64_t)fdiv(row, bm) * a.scale_cols + fdiv(cin, cpb);
+  if constexpr (DQ == kDqFp8) {
+    return static_cast<const float*>(a.scales)[si];
+  } else if constexpr (DQ == kDqMx) {
+    const uint32_t e = static_cast<const uint8_t*>(a.scales)[si];
+    return e == 255 ? __int_as_float(0x7F800000) : exp2i((int)e - 127);
+  } else if constexpr (DQ == kDqNv) {
+    return dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
+  } else {
+    has_zp = a.zp != nullptr;
+    if (a.scale_f16) {
+      if (has_zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
+      return __half2float(static_cast<const __half*>(a.scales)[si]);
+    }
+    if (has_zp) zp = static_cast<const float*>(a.zp)[si];
+    return static_cast<const float*>(a.scales)[si];
+  }
+}
+
+// A warp walks spans of 512 codes; in each, lane t takes codes 4t..4t+3 of
+// every 128-code quarter, so each warp-wide 4-byte load reads 128
+// contiguous bytes and each store writes 512 (float32) or 256 (bf16/f16)
+// contiguous bytes. The chunk's row and scale index come from 32-bit
+// multiply-shift divisions (chunks per row, block height, chunks per block).
 template <int DQ, int FMT, int OUT>
-__global__ void __launch_bounds__(256) k_dequant(DequantArgs a) {
+__global__ void __launch_bounds__(256) k_dequant(DequantArgs a, FastDiv cpr, FastDiv bm,
+                                                 FastDiv cpb) {
+  const uint32_t ngroups = (uint32_t)(a.n / 4);  // 4-code groups (n % 16 == 0)
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
+  float pscale = 0.f;
+  if constexpr (DQ == kDqFp8) {
+    if (a.per_tensor) pscale = *static_cast<const float*>(a.scales);
+  }
+  for (uint32_t span = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       (uint64_t)span * 128 < ngroups; span += nwarps) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t g = span * 128 + 32 * j + lane;
+      w[j] = g < ngroups ? ldg4(a.codes + (int64_t)g * 4) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t g = span * 128 + 32 * j + lane;
+      if (g >= ngroups) break;
+      float zp = 0.f;
+      bool has_zp = false;
+      float scale = pscale;
+      if (!(DQ == kDqFp8 && a.per_tensor)) scale = chunk_scale<DQ>(a, g >> 2, cpr, bm, cpb, zp, has_zp);
+      float v[4];
+      decode4<DQ, FMT>(w[j], v, a.is_signed, has_zp, zp);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], scale);
+      if constexpr (OUT == BRC_DTYPE_F32) {
+        stg16(static_cast<float*>(a.out) + (int64_t)g * 4,
+              make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                         __float_as_uint(v[3])));
+      } else {
+        uint32_t h0, h1;
+        if constexpr (OUT == BRC_DTYPE_BF16) {
+          const __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
+          const __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
+          h0 = *reinterpret_cast<const uint32_t*>(&p0);
+          h1 = *reinterpret_cast<const uint32_t*>(&p1);
+        } else {
+          const __half2 p0 = __floats2half2_rn(v[0], v[1]);
+          const __half2 p1 = __floats2half2_rn(v[2], v[3]);
+          h0 = *reinterpret_cast<const uint32_t*>(&p0);
+          h1 = *reinterpret_cast<const uint32_t*>(&p1);
+        }
+        stg8(static_cast<char*>(a.out) + (int64_t)g * 8, h0, h1);
+      }
+    }
+  }
+}
+
+// Tensors of 2^31 chunks (2^35 elements) or more: 64-bit indices.
+template <int DQ, int FMT, int OUT>
+__global__ void __launch_bounds__(256) k_dequant_wide(DequantArgs a) {
   const int64_t nchunks = a.n / 16;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
        c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e0 = c * 16;
     const uint4 cv = ldg16(a.codes + e0);
-    const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
     float scale = 0.f, zp = 0.f;
+    bool has_zp = false;
     if (a.per_tensor) {
       scale = *static_cast<const float*>(a.scales);
     } else {
@@ -903,22 +1056,14 @@ __global__ void __launch_bounds__(256) k_dequant(DequantArgs a) {
           scale = static_cast<const float*>(a.scales)[si];
           if (a.zp) zp = static_cast<const float*>(a.zp)[si];
         }
+        has_zp = a.zp != nullptr;
       }
     }
+    const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
     float v[16];
+    decode16<DQ, FMT>(w, v, a.is_signed, has_zp, zp);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t code = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-      float d;
-      if constexpr (DQ == kDqFp8 || DQ == kDqMx) d = dec_fp8<FMT>(code);
-      else if constexpr (DQ == kDqNv) d = dec_e2m1(code);
-      else {
-        const uint32_t lo = code & 0xFu;
-        d = (a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
-        if (a.zp) d = __fsub_rn(d, zp);
-      }
-      v[i] = __fmul_rn(d, scale);
-    }
+    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], scale);
     store_out16<OUT>(a.out, e0, v);
   }
 }
@@ -1460,9 +1605,21 @@ namespace {
 template <int DQ, int FMT>
 int launch_dequant(const DequantArgs& a, int out_dtype, cudaStream_t st) {
   const int grid = grid_for(a.n / 16 + 1, 256 * 2);
-  if (out_dtype == BRC_DTYPE_F32) k_dequant<DQ, FMT, BRC_DTYPE_F32><<<grid, 256, 0, st>>>(a);
-  else if (out_dtype == BRC_DTYPE_BF16) k_dequant<DQ, FMT, BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(a);
-  else k_dequant<DQ, FMT, BRC_DTYPE_F16><<<grid, 256, 0, st>>>(a);
+  const int64_t cpr = a.cols / 16, cpb = a.block_k / 16;
+  if (a.n / 4 >= (1ll << 31) || cpr >= (1ll << 31)) {
+    if (out_dtype == BRC_DTYPE_F32) k_dequant_wide<DQ, FMT, BRC_DTYPE_F32><<<grid, 256, 0, st>>>(a);
+    else if (out_dtype == BRC_DTYPE_BF16)
+      k_dequant_wide<DQ, FMT, BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(a);
+    else k_dequant_wide<DQ, FMT, BRC_DTYPE_F16><<<grid, 256, 0, st>>>(a);
+    return check_launch();
+  }
+  const FastDiv fcpr = make_fastdiv((uint32_t)cpr), fbm = make_fastdiv((uint32_t)a.block_m),
+                fcpb = make_fastdiv((uint32_t)cpb);
+  if (out_dtype == BRC_DTYPE_F32)
+    k_dequant<DQ, FMT, BRC_DTYPE_F32><<<grid, 256, 0, st>>>(a, fcpr, fbm, fcpb);
+  else if (out_dtype == BRC_DTYPE_BF16)
+    k_dequant<DQ, FMT, BRC_DTYPE_BF16><<<grid, 256, 0, st>>>(a, fcpr, fbm, fcpb);
+  else k_dequant<DQ, FMT, BRC_DTYPE_F16><<<grid, 256, 0, st>>>(a, fcpr, fbm, fcpb);
   return check_launch();
 }
 
