@@ -34,10 +34,20 @@
 // warp streams the CTA's tiles (row block by row block, one activation chunk
 // at a time; the chunk is the whole K when it fits in shared memory) through
 // a ring of large stages of 32 tiles (about 37 KB, three bulk copies when
-// the tiles are contiguous), and loads the activation chunks. Each of the 16
-// consumer warps takes two consecutive tiles (two groups of one row block)
-// of every stage; partial sums of a row block meet in shared memory. Stages are released through "empty" mbarriers (one
-// arrival per consumer warp). Every wait is bounded: on a timeout the waiter
+// the tiles are contiguous), and loads the activation chunks. Two ways to
+// split a stage among the 16 consumer warps:
+//  * shared (a row block's chunk spans more than a stage: M <= 4 at K = 8192,
+//    whole K resident): each warp takes two consecutive tiles (two groups of
+//    one row block) of every stage; partial sums of a row block meet in
+//    shared memory;
+//  * owner (a stage holds whole row blocks of the chunk: the chunked
+//    activations of M > 4): each warp owns the CTA's row blocks w and w + 16,
+//    keeps their sums in registers across every chunk and writes them at the
+//    end. With the shared split a chunk of 8 groups moved each warp to a new
+//    row block every stage, and the shared-memory partial-sum atomics took
+//    about 30% of the time (C5 M = 16: 84 -> 63 us).
+// Stages are released through "empty" mbarriers (one arrival per consumer
+// warp in both modes: an owner passes the stages it has no tile in). Every wait is bounded: on a timeout the waiter
 // records the status bit and raises the CTA's abort flag; the others see the
 // flag, stop, and the producer waits for its copies in flight.
 
@@ -202,7 +212,15 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
   return mbar_wait(bar, parity, abort_flag, status, 1u);
 }
 
-template <int MT, int MODE, int OUT, int NC>  // MODE 0: unsigned sym, 1: signed sym, 2: asym
+// OWNER (used when a stage holds whole row blocks of a chunk, 32 % gpc == 0):
+// consumer warp w owns the CTA's row blocks w, w + NC; it walks every stage
+// of every chunk in order (waiting on it and releasing it, so the ring's
+// barrier counts are those of the shared mode) but does the math only for
+// its own row blocks, keeps their sums in registers across all chunks, and
+// writes them to global memory at the end: no shared-memory partial sums.
+// Otherwise every warp takes TPW tiles of every stage and row-block partial
+// sums meet in shared memory.
+template <int MT, int MODE, int OUT, int NC, bool OWNER>  // MODE 0: unsigned sym, 1: signed sym, 2: asym
 __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int kConsumers = NC, kThreads = threads_for(NC), STAGE_TILES = NC * TPW;
@@ -373,6 +391,13 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[mt][i] = 0.f;
+  float own[2][MT][4];  // OWNER: sums of this warp's row blocks warp and warp + NC
+#pragma unroll
+  for (int o = 0; o < 2; ++o)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) own[o][mt][i] = 0.f;
 
   auto flush = [&](int rbl) {  // this warp's partial sums of row block rbl -> shared
 #pragma unroll
@@ -418,6 +443,53 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
       }
     }
     consumers_sync<NC>();  // the chunk's sums are visible
+
+    if constexpr (OWNER) {
+      const int rbs = STAGE_TILES / gpc;  // row blocks per stage
+      for (int k = 0; ok && k < nst; ++k) {
+        if (!wait_or_abort(&full[slot], phase, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* sp = ring + (size_t)slot * STAGE_BYTES;
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+          const int rb = warp + o * NC;
+          if (rb < nrb && rb / rbs == k) {
+            const int base = (rb - k * rbs) * gpc;  // first tile of the row block in the stage
+            for (int j = 0; j < gpc; ++j) {
+              const int pos = base + j;
+              const uint4 w0 = *reinterpret_cast<const uint4*>(sp + pos * TILE_BYTES + gid * 64 +
+                                                               16 * t);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(sp + pos * TILE_BYTES +
+                                                               (gid + 8) * 64 + 16 * t);
+              const float2 sc = *reinterpret_cast<const float2*>(sp + STAGE_TILES * TILE_BYTES +
+                                                                 pos * 64 + gid * 8);
+              float2 off;
+              if constexpr (MODE == 2)
+                off = *reinterpret_cast<const float2*>(sp + STAGE_TILES * (TILE_BYTES + 64) +
+                                                       pos * 64 + gid * 8);
+              else
+                off = MODE == 1 ? make_float2(136.f, 136.f) : make_float2(128.f, 128.f);
+              const __nv_bfloat16* bg[MT];
+#pragma unroll
+              for (int mt = 0; mt < MT; ++mt)
+                bg[mt] = As + (size_t)(mt * 8 + gid) * rs + 32 * t + j * G;
+              tile_math<MT, MODE>(own[o], w0, w1, sc, off, bg, brow_ok, SAs + j * 16, t);
+            }
+          }
+        }
+        __syncwarp();  // every lane is done reading the slot
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == R) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aempty[b]);  // done with this chunk's activations
+      continue;
+    }
 
     const __nv_bfloat16* brow[MT];
 #pragma unroll
@@ -482,6 +554,28 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
     __syncwarp();
     if (lane == 0) mbar_arrive(&aempty[b]);  // done with this chunk's activations
   }
+  if constexpr (OWNER) {
+    if (!ok || *abort_flag) return;
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      const int rb = warp + o * NC;
+      if (rb >= nrb) continue;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int m = mt * 8 + 2 * t + (i & 1);
+          if (m >= p.M) continue;
+          const int64_t o_ = (int64_t)m * p.N + (int64_t)(rb0 + rb) * 16 + gid + (i >> 1) * 8;
+          const float v = own[o][mt][i];
+          if constexpr (OUT == BRC_DTYPE_F32) static_cast<float*>(p.out)[o_] = v;
+          else if constexpr (OUT == BRC_DTYPE_BF16)
+            static_cast<__nv_bfloat16*>(p.out)[o_] = __float2bfloat16_rn(v);
+          else static_cast<__half*>(p.out)[o_] = __float2half_rn(v);
+        }
+    }
+    return;
+  }
   consumers_sync<NC>();  // all partial sums are in shared memory
   if (*abort_flag) return;
   const int cols = nrb * 16;
@@ -497,10 +591,10 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
 }
 
 // ------------------------------------------------------------------ host
-template <int MT, int MODE, int OUT>
+template <int MT, int MODE, int OUT, bool OWNER>
 int launch(const Params& p, int grid, size_t smem, cudaStream_t st) {
   constexpr int NC = consumers_for(MT);
-  auto kern = k_int4_skinny<MT, MODE, OUT, NC>;
+  auto kern = k_int4_skinny<MT, MODE, OUT, NC, OWNER>;
   // the opt-in shared-memory size is set once per device (to the maximum)
   static bool configured[64] = {};
   static std::mutex mu;
@@ -519,19 +613,20 @@ int launch(const Params& p, int grid, size_t smem, cudaStream_t st) {
   return check_launch();
 }
 
-template <int MT, int MODE>
+template <int MT, int MODE, bool OWNER>
 int launch_out(int out_dtype, const Params& p, int grid, size_t smem, cudaStream_t st) {
-  if (out_dtype == BRC_DTYPE_F32) return launch<MT, MODE, BRC_DTYPE_F32>(p, grid, smem, st);
-  if (out_dtype == BRC_DTYPE_BF16) return launch<MT, MODE, BRC_DTYPE_BF16>(p, grid, smem, st);
-  return launch<MT, MODE, BRC_DTYPE_F16>(p, grid, smem, st);
+  if (out_dtype == BRC_DTYPE_F32) return launch<MT, MODE, BRC_DTYPE_F32, OWNER>(p, grid, smem, st);
+  if (out_dtype == BRC_DTYPE_BF16)
+    return launch<MT, MODE, BRC_DTYPE_BF16, OWNER>(p, grid, smem, st);
+  return launch<MT, MODE, BRC_DTYPE_F16, OWNER>(p, grid, smem, st);
 }
 
-template <int MT>
+template <int MT, bool OWNER>
 int launch_mode(int mode, int out_dtype, const Params& p, int grid, size_t smem,
                 cudaStream_t st) {
-  if (mode == 0) return launch_out<MT, 0>(out_dtype, p, grid, smem, st);
-  if (mode == 1) return launch_out<MT, 1>(out_dtype, p, grid, smem, st);
-  return launch_out<MT, 2>(out_dtype, p, grid, smem, st);
+  if (mode == 0) return launch_out<MT, 0, OWNER>(out_dtype, p, grid, smem, st);
+  if (mode == 1) return launch_out<MT, 1, OWNER>(out_dtype, p, grid, smem, st);
+  return launch_out<MT, 2, OWNER>(out_dtype, p, grid, smem, st);
 }
 
 // Shared-memory plan for one call: activation chunk and ring depth.
@@ -612,6 +707,14 @@ extern "C" int brc_gemm_int4(const void* a_bf16, int M, int K, const uint8_t* w_
   p.status = brc::gemm_status_ptr();
   const int mode = symmetric ? (is_signed ? 1 : 0) : 2;
   cudaStream_t st = (cudaStream_t)stream;
-  return M <= 8 ? launch_mode<1>(mode, d_dtype, p, grid, pl.L.total, st)
-                : launch_mode<2>(mode, d_dtype, p, grid, pl.L.total, st);
+  // row-block owners when a stage holds whole row blocks of a chunk (and a
+  // warp owns at most two row blocks)
+  const int gpc = pl.kc / G;
+  const bool owner = (consumers_for(M <= 8 ? 1 : 2) * TPW) % gpc == 0 &&
+                     rbmax <= 2 * consumers_for(M <= 8 ? 1 : 2);
+  if (owner)
+    return M <= 8 ? launch_mode<1, true>(mode, d_dtype, p, grid, pl.L.total, st)
+                  : launch_mode<2, true>(mode, d_dtype, p, grid, pl.L.total, st);
+  return M <= 8 ? launch_mode<1, false>(mode, d_dtype, p, grid, pl.L.total, st)
+                : launch_mode<2, false>(mode, d_dtype, p, grid, pl.L.total, st);
 }
