@@ -133,12 +133,14 @@ struct LaneVals {
 // cast_ste output for one lane: each code's dequantized value y (decode x
 // the stored scale; asymmetric INT4 (q - zp) x scale, as cast.py:574-586) and
 // x + (y - x) in float32, as the reference's x + (y - x).detach() evaluates it.
+// The values go straight to this lane's slot of the warp's shared-memory
+// stage (16 bytes at a time), so no register array holds them.
 template <int MODE, int FMT, int NW>
-__device__ __forceinline__ void ste_store(const BlockCastArgs& a, int64_t e0, const float* f,
-                                          const uint32_t* w, float dqs, float dqz) {
-  float o[4 * NW];
+__device__ __forceinline__ void ste_values(const BlockCastArgs& a, const float* f,
+                                           const uint32_t* w, float dqs, float dqz, float* o) {
 #pragma unroll
   for (int j = 0; j < NW; ++j) {
+    float q[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t code = (w[j] >> (8 * i)) & 0xFFu;
@@ -153,13 +155,34 @@ __device__ __forceinline__ void ste_store(const BlockCastArgs& a, int64_t e0, co
         if constexpr (MODE == kInt4Asym) d = __fsub_rn(d, dqz);
       }
       const float x = f[4 * j + i];
-      o[4 * j + i] = __fadd_rn(x, __fsub_rn(__fmul_rn(d, dqs), x));
+      q[i] = __fadd_rn(x, __fsub_rn(__fmul_rn(d, dqs), x));
+    }
+    *reinterpret_cast<float4*>(o + 4 * j) = make_float4(q[0], q[1], q[2], q[3]);
+  }
+}
+
+// The warp's cast_ste values go out through a per-warp shared-memory
+// transpose: lane l has written its E consecutive values (elements l * E ..
+// l * E + E of the warp's tile, which is contiguous in memory) to row l of
+// `stage` (32 rows of E + 4 floats); stores of 16 bytes per lane at lane
+// stride E * 4 bytes would each touch 32 separate lines, while after the
+// transpose every warp store writes 512 contiguous bytes. Every lane of the
+// warp calls this; elements past the tensor's end are not stored.
+template <int E>
+__device__ __forceinline__ void ste_warp_store(const BlockCastArgs& a, int64_t tile_e0,
+                                               int64_t n_elems, const float* stage) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < E / 4; ++q) {
+    const int e = q * 128 + 4 * lane;  // element of the warp's tile
+    if (tile_e0 + e < n_elems) {
+      const float4 v = *reinterpret_cast<const float4*>(stage + (e / E) * (E + 4) + e % E);
+      stg16(a.ste_out + tile_e0 + e, make_uint4(__float_as_uint(v.x), __float_as_uint(v.y),
+                                                __float_as_uint(v.z), __float_as_uint(v.w)));
     }
   }
-#pragma unroll
-  for (int k = 0; k < 4 * NW; k += 4)
-    stg16(a.ste_out + e0 + k, make_uint4(__float_as_uint(o[k]), __float_as_uint(o[k + 1]),
-                                         __float_as_uint(o[k + 2]), __float_as_uint(o[k + 3])));
+  __syncwarp();  // the stage is rewritten by the next tile
 }
 
 // Encode one lane's E values given the block's scale; writes codes/packed
@@ -167,7 +190,8 @@ __device__ __forceinline__ void ste_store(const BlockCastArgs& a, int64_t e0, co
 template <int MODE, int FMT, int E, bool STE = false>
 __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, const float* f,
                                             float s, float zp, bool fast, int64_t tile_off,
-                                            float dqs = 0.f, float dqz = 0.f) {
+                                            float dqs = 0.f, float dqz = 0.f,
+                                            float* ste = nullptr) {
   constexpr int NW = E / 4;
   uint32_t w[NW];
   if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
@@ -194,7 +218,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
       }
     }
     if constexpr (STE) {
-      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      ste_values<MODE, FMT, NW>(a, f, w, dqs, dqz, ste);
       return;
     }
     store_words<NW>(a.codes + e0, w);
@@ -214,7 +238,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
       }
     }
     if constexpr (STE) {
-      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      ste_values<MODE, FMT, NW>(a, f, w, dqs, dqz, ste);
       return;
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
@@ -258,7 +282,7 @@ __device__ __forceinline__ void encode_lane(const BlockCastArgs& a, int64_t e0, 
       }
     }
     if constexpr (STE) {
-      ste_store<MODE, FMT, NW>(a, e0, f, w, dqs, dqz);
+      ste_values<MODE, FMT, NW>(a, f, w, dqs, dqz, ste);
       return;
     }
     if (a.codes) store_words<NW>(a.codes + e0, w);
@@ -298,6 +322,10 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
       for (int i = 0; i < NV; ++i) dst[i] = ldg16(src + 16 * i);
     }
   };
+  // cast_ste: per-warp transpose area for coalesced float32 stores (8 warps)
+  __shared__ __align__(16) float ste_stage[STE ? 8 * 32 * (E + 4) : 4];
+  float* my_stage = ste_stage + (STE ? (threadIdx.x >> 5) * 32 * (E + 4) : 0);
+  float* my_row = my_stage + (STE ? lane * (E + 4) : 0);
   load_tile(tile, vn);
   for (; tile < n_tiles; tile += n_warps) {
     const int64_t blk = tile * BPW + lane / LPB;
@@ -331,8 +359,8 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
         st0 = fmax_nan(st0, __shfl_xor_sync(0xFFFFFFFFu, st0, o));
       }
     }
-    if (!valid) continue;
-
+    if (!valid && !STE) continue;
+    if (valid) {
     float f[E];
 #pragma unroll
     for (int i = 0; i < NV; ++i) unpack<DT>(v[i], f + i * V);
@@ -430,7 +458,9 @@ __global__ void __launch_bounds__(256) k_block_cast(BlockCastArgs a) {
         }
       }
     }
-    encode_lane<MODE, FMT, E, STE>(a, e0, f, s, zp, fast, tile_off, dqs, dqz);
+    encode_lane<MODE, FMT, E, STE>(a, e0, f, s, zp, fast, tile_off, dqs, dqz, my_row);
+    }  // valid
+    if constexpr (STE) ste_warp_store<E>(a, tile * BPW * B, a.n_blocks * B, my_stage);
   }
 }
 
