@@ -87,6 +87,8 @@ def parse():
     ap.add_argument("--no-per-recipe", action="store_true")
     ap.add_argument("--no-sharded", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the headline step as eager launches instead of a CUDA graph")
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="rows of A / W^T the CPU port encodes per sample (default 64 for "
                          "cpu_baseline, 16 per step for --impl reference)")
@@ -489,9 +491,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     job_flops = FLOPS * (world if batch else 1)
 
-    gemm_events = []
-
-    def step(a_in, w_in, record=False):
+    def step(a_in, w_in, marks=None):
         if batch:
             # activations: global amax over all ranks' batches, its all-reduce
             # in flight while the (replicated) weight is cast
@@ -500,19 +500,48 @@ def run_ours(args):
             sa = pending.wait()
         else:
             sa, sw = cast_weight_split(a_in, w_in, recipe)
-        if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
+        if marks is not None:
+            marks[0].record()
         out = bb.linear(sa, sw, out_dtype=torch.bfloat16)
-        if record:
-            e1.record()
-            gemm_events.append((e0, e1))
+        if marks is not None:
+            marks[1].record()
         return out
 
     # ---- device-resident timing
     for _ in range(args.warmup):
         out = step(A, Wt_sh)
+    _barrier()
+    # One step is captured as a CUDA graph (its 7 kernels and, with N > 1, its
+    # NCCL all-reduce) and replayed. Issued from Python the step costs the host
+    # more than the device once the GEMM is split 8 ways (8 ranks' processes
+    # share the host), so the GPUs would idle between launches. Every rank
+    # agrees on graph or eager timing before any replay.
+    graph, timing = None, "eager launches from Python"
+    # events around the GEMM inside the step (in the graph: event record nodes)
+    marks = None
+    if not args.eager:
+        err = ""
+        try:
+            marks = (torch.cuda.Event(enable_timing=True, external=True),
+                     torch.cuda.Event(enable_timing=True, external=True))
+            graph = torch.cuda.CUDAGraph()
+            cs = torch.cuda.Stream()
+            cs.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cs):
+                with torch.cuda.graph(graph, stream=cs):
+                    out = step(A, Wt_sh, marks)
+            torch.cuda.current_stream().wait_stream(cs)
+            torch.cuda.synchronize()
+        except Exception as e:  # capture refused on this rank
+            graph, err = None, f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"
+        if _max_over_ranks([0.0 if graph is not None else 1.0])[0] > 0:
+            graph = None
+            out = step(A, Wt_sh)
+            timing = "eager launches from Python (CUDA-graph capture failed: " + (err or "on another rank") + ")"
+        else:
+            graph.replay()
+            timing = ("one step captured as a CUDA graph (7 kernels" +
+                      (" + 1 NCCL all-reduce" if world > 1 else "") + "), replayed per step")
     _barrier()
     props = torch.cuda.get_device_properties(dev)
     uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else None
@@ -521,12 +550,26 @@ def run_ours(args):
     with Clocks(uuid) as clk:
         t_start.record()
         for _ in range(args.steps):
-            out = step(A, Wt_sh, record=True)
+            if graph is not None:
+                graph.replay()
+            else:
+                out = step(A, Wt_sh)
         t_end.record()
         torch.cuda.synchronize()
     _barrier()
     ms = t_start.elapsed_time(t_end) / args.steps
-    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gemm_events)
+    # the GEMM inside the step: the events around it, read after single steps
+    samples = []
+    for _ in range(min(10, max(3, args.steps))):
+        if graph is not None:
+            graph.replay()
+        else:
+            marks = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            out = step(A, Wt_sh, marks)
+        torch.cuda.synchronize()
+        samples.append(marks[0].elapsed_time(marks[1]))
+    gemm_ms = statistics.median(samples)
+    _barrier()
     ms, gemm_ms_max = _max_over_ranks([ms, gemm_ms])
     value = job_flops / (ms * 1e-3) / 1e12
 
@@ -534,6 +577,9 @@ def run_ours(args):
     if not args.no_parity:
         parity = headline_parity(A, Wt_sh, out, recipe) if not batch else None
     del out
+    if graph is not None:  # released before the process group (it holds an NCCL call)
+        del graph
+        torch.cuda.synchronize()
 
     # ---- end to end through the public API, host buffers
     # Every step copies its own inputs from pinned host memory and its result
@@ -652,6 +698,7 @@ def run_ours(args):
             "data": "synthetic (seeded torch generator, BASELINE configs[1] shapes/distributions)",
             "config": headline_config(world, args.shard),
             "clocks": clk.summary(),
+            "timing": timing,
             "e2e": e2e,
             "gpu_launches": 7 * args.steps * world,
             "gpu_launches_per_rank_per_step": {"amax_reset": 2, "amax": 2, "encode": 2, "gemm": 1},
