@@ -31,6 +31,7 @@ PROTOTYPES = {
     "brc_cast_pertensor_fp8_apply": ([_p, _i, _i64, _i, _p, _p, _p, _p], _i),
     "brc_cast_pertensor_fp8": ([_p, _i, _i64, _i, _p, _p, _p, _p], _i),
     "brc_cast_pertensor_fp8_noalloc": ([_p, _i, _i64, _i, _p, _p, _p], _i),
+    "brc_cast_pertensor_fp8_delayed": ([_p, _i, _i64, _i, _p, _i, _i, _i, _p, _p, _p, _p], _i),
     "brc_cast_block_fp8": ([_p, _i, _i64, _i64, _i, _i, _p, _p, _p], _i),
     "brc_cast_block_fp8_2d": ([_p, _i, _i64, _i64, _i, _i, _i, _p, _p, _p], _i),
     "brc_cast_mxfp8": ([_p, _i, _i64, _i64, _i, _p, _p, _p, _p], _i),

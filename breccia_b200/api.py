@@ -35,7 +35,7 @@ from . import _lib
 from . import types as T
 
 __all__ = ["cast", "dequantize", "requantize", "matmul", "linear", "gemm_operands",
-           "attach_gemm_operands"]
+           "attach_gemm_operands", "AmaxHistory"]
 
 _TORCH_FP8 = {"E4M3": torch.float8_e4m3fn, "E5M2": torch.float8_e5m2}
 _FMT = {"E4M3": _lib.FP8_E4M3, "E5M2": _lib.FP8_E5M2}
@@ -148,13 +148,49 @@ def _mma_scale_shape(rows: int, scale_cols: int):
 # ------------------------------------------------------------------- cast
 
 
-def cast(x: Any, recipe: Any, *, block_m: Optional[int] = None):
+class AmaxHistory:
+    """DelayedScaling state of one tensor across steps (extension).
+
+    breccia's ``DelayedScaling`` carries ``amax_history_len`` and ``margin``
+    (``recipes.py:43-77``) but its cast uses the current amax (``cast.py:
+    364-373``). Passed to ``cast(x, DelayedScaling(...), amax_history=h)``,
+    this object makes the cast use them, as TransformerEngine's delayed
+    scaling does: ``history`` is a float32 ring of the last amaxes on the
+    device (most recent first) and ``recorded`` counts the casts that wrote
+    into it (kept on the host, so no device read is needed to choose).
+
+    * While nothing is recorded the cast is the reference's current-amax cast,
+      bit for bit, and records that amax.
+    * Afterwards the scale comes from the ring before the tensor is read,
+      ``float32(max(max(history), 1e-10) / fmt_max) * 2**margin``, and the
+      cast is one pass (each element read once instead of twice); values
+      beyond the scaled range saturate; the tensor's amax is recorded.
+    """
+
+    def __init__(self, length: int = 16, device: Any = None):
+        if length < 1:
+            raise ValueError(f"amax history length must be >= 1, got {length}")
+        self.history = torch.zeros(length, dtype=torch.float32,
+                                   device=device if device is not None else "cuda")
+        self.recorded = 0
+
+    def reset(self) -> None:
+        self.history.zero_()
+        self.recorded = 0
+
+
+def cast(x: Any, recipe: Any, *, block_m: Optional[int] = None,
+         amax_history: Optional[AmaxHistory] = None):
     """Quantize a CUDA tensor with ``recipe`` (``cast.py:64-92``).
 
     ``block_m`` (extension, ``Float8BlockScaling`` only): scale
     ``block_m x block_k`` tiles of the last two axes instead of ``1 x block_k``
     runs -- the DeepSeek-v3 128x128 weight layout, ``PerBlockMN(block_m,
     block_k)``. The reference can describe but not produce it.
+
+    ``amax_history`` (extension, ``DelayedScaling`` only): an
+    :class:`AmaxHistory` that carries the recipe's amax history and margin
+    across calls (one-pass casts once it holds an amax).
     """
     x = _input(x)
     ST, L = _classes(recipe)
@@ -162,6 +198,10 @@ def cast(x: Any, recipe: Any, *, block_m: Optional[int] = None):
     dev = x.device
     with torch.cuda.device(dev):
         st = _stream(dev)
+        if amax_history is not None:
+            if name != "delayed":
+                raise ValueError("amax_history applies to DelayedScaling only")
+            return _cast_delayed(x, recipe, ST, L, st, amax_history)
         if name in ("delayed", "current"):
             return _cast_per_tensor(x, recipe, ST, L, st)
         if name == "block":
@@ -182,6 +222,22 @@ def _cast_per_tensor(x, recipe, ST, L, st):
     ws = torch.empty(1, dtype=torch.int32, device=x.device)
     _lib.call("brc_cast_pertensor_fp8", x.data_ptr(), _IN_DT[x.dtype], x.numel(), _FMT[fmt],
               codes.data_ptr(), scale.data_ptr(), ws.data_ptr(), st)
+    return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe, layout=L.PerTensor())
+
+
+def _cast_delayed(x, recipe, ST, L, st, h):
+    fmt = recipe.fp8_format
+    hist = h.history
+    if not (isinstance(hist, torch.Tensor) and hist.is_cuda and hist.dtype == torch.float32 and
+            hist.is_contiguous() and hist.device == x.device):
+        raise TypeError("AmaxHistory.history must be a contiguous float32 tensor on x's device")
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    ws = torch.empty(1, dtype=torch.int32, device=x.device)
+    _lib.call("brc_cast_pertensor_fp8_delayed", x.data_ptr(), _IN_DT[x.dtype], x.numel(),
+              _FMT[fmt], hist.data_ptr(), hist.numel(), int(recipe.margin),
+              1 if h.recorded > 0 else 0, codes.data_ptr(), scale.data_ptr(), ws.data_ptr(), st)
+    h.recorded += 1
     return ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe, layout=L.PerTensor())
 
 

@@ -14,6 +14,7 @@
 // keep the per-element instruction count low enough (~10-14 ops) that a
 // 2-byte input stays bandwidth-bound.
 
+#include <cmath>
 #include <mutex>
 
 #include "common.cuh"
@@ -1934,4 +1935,159 @@ extern "C" int brc_cast_pertensor_fp8_noalloc(const void* x, int x_dtype, int64_
   if (rc) return rc;
   return dispatch_dt_fmt<NoAllocCast>(x_dtype, fmt, x, n, codes, scale_out, scratch,
                                       (cudaStream_t)stream);
+}
+
+// ========================================================================
+// DelayedScaling with an amax history (extension; the reference's cast
+// ignores the recipe's amax_history_len / margin: recipes.py:43-77,
+// cast.py:364-373). The history is a caller-owned float32 ring on the
+// device, most recent first. A cast that uses it takes its dequantization
+// scale from the history before reading the tensor,
+//   s = float32(max(max(history), 1e-10) / fmt_max) * 2^margin  (float32),
+// so it is ONE pass: each element is read once, encoded with s (the same
+// clip-then-encode and IEEE division as the current-amax cast) while the
+// tensor's own amax is reduced, and that amax is pushed into the ring
+// afterwards. A cast without history (the caller's first) is the current-
+// amax cast of the reference, bit for bit, and records its amax.
+// ========================================================================
+namespace brc {
+namespace delayed {
+
+template <int FMT>
+__global__ void k_history_scale(const float* __restrict__ hist, int len, float margin_pow2,
+                                float floor_scale, float* scale_out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
+  float m = 0.f;
+  for (int i = 0; i < len; ++i) m = fmax_nan(m, fabsf(hist[i]));
+  const float s = __fmul_rn(pertensor_scale(__float_as_uint(m), kMax, floor_scale), margin_pow2);
+  *scale_out = canon_nan(s);
+}
+
+// Encode with a scale known before the pass; reduce the tensor's amax on the
+// way (NaN propagates; the float bits of a non-negative value or NaN order
+// as integers, so atomicMax on the bits is the float maximum).
+template <int DT, int FMT>
+__global__ void __launch_bounds__(256) k_delayed_apply(const void* __restrict__ x, int64_t n,
+                                                       const float* scale_in, uint8_t* codes,
+                                                       uint32_t* amax_bits) {
+  constexpr int V = In<DT>::kVec;
+  const float s = *scale_in;
+  const bool fast = isfinite(s) && s > 0.f;
+  const float r = __frcp_rn(s);
+  const int64_t nvec = n / V;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const char* base = static_cast<const char*>(x);
+  float m = 0.f;
+  auto encode_store = [&](const uint4 v, int64_t vi) {
+    const float vmax = vec_absmax<DT>(v);
+    m = fmax_nan(m, vmax);
+    float f0[V];
+    unpack<DT>(v, f0);
+    uint32_t w0[V / 4];
+    // The scale is finite while the tensor may hold NaN (the current-amax
+    // cast never meets this: a NaN makes its scale NaN). The fast encoder
+    // clamps with fminf, which maps NaN to the maximum code, so a vector
+    // holding a NaN takes the per-element path (NaN -> the NaN code).
+    if (fast && !isnan(vmax)) {
+#pragma unroll
+      for (int j = 0; j < V / 4; ++j)
+        w0[j] = enc4_fp8<FMT>(div_by(f0[4 * j], s, r), div_by(f0[4 * j + 1], s, r),
+                              div_by(f0[4 * j + 2], s, r), div_by(f0[4 * j + 3], s, r));
+    } else {
+#pragma unroll
+      for (int j = 0; j < V / 4; ++j) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f0[4 * j + i], s)) << (8 * i);
+        w0[j] = c;
+      }
+    }
+    if constexpr (V == 8) {
+      *reinterpret_cast<uint2*>(codes + vi * V) = make_uint2(w0[0], w0[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(codes + vi * V) = w0[0];
+    }
+  };
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = ldg16(base + 16 * (i + u * stride));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) encode_store(v[u], i + u * stride);
+  }
+  for (; i < nvec; i += stride) encode_store(ldg16(base + 16 * i), i);
+  for (int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride) {
+    const float xv = load1<DT>(x, t);
+    m = fmax_nan(m, fabsf(xv));
+    codes[t] = (uint8_t)enc1_fp8<FMT>(div_ieee(xv, s));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (threadIdx.x == 0 && __float_as_uint(m) != 0u) atomicMax(amax_bits, __float_as_uint(m));
+  }
+}
+
+// Ring update: the entries move one place back and the new amax goes first.
+__global__ void k_history_push(float* hist, int len, const uint32_t* amax_bits) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  for (int i = len - 1; i > 0; --i) hist[i] = hist[i - 1];
+  hist[0] = canon_nan(__uint_as_float(*amax_bits));
+}
+
+}  // namespace delayed
+}  // namespace brc
+
+namespace {
+template <int DT, int FMT>
+struct DelayedCast {
+  static int run(const void* x, int64_t n, float* hist, int len, int margin, uint8_t* codes,
+                 float* scale_out, uint32_t* ws, cudaStream_t st) {
+    using namespace brc::delayed;
+    const double fmax = FMT == BRC_FP8_E4M3 ? 448.0 : 57344.0;
+    const float floor_scale = (float)(1e-10 / fmax);
+    k_history_scale<FMT><<<1, 32, 0, st>>>(hist, len, std::ldexp(1.0f, margin), floor_scale,
+                                           scale_out);
+    int rc = check_launch();
+    if (rc) return rc;
+    if ((rc = brc_amax_reset(ws, st))) return rc;
+    if (n > 0) {
+      const int V = In<DT>::kVec;
+      k_delayed_apply<DT, FMT><<<grid_for(n / V + 1, 256 * 4), 256, 0, st>>>(x, n, scale_out,
+                                                                          codes, ws);
+      if ((rc = check_launch())) return rc;
+    }
+    k_history_push<<<1, 32, 0, st>>>(hist, len, ws);
+    return check_launch();
+  }
+};
+}  // namespace
+
+extern "C" int brc_cast_pertensor_fp8_delayed(const void* x, int x_dtype, int64_t n, int fmt,
+                                              float* history, int history_len, int margin,
+                                              int use_history, uint8_t* codes, float* scale_out,
+                                              uint32_t* workspace, void* stream) {
+  if (!history || !scale_out || !workspace || ((!x || !codes) && n > 0)) return BRC_ERR_NULL;
+  if (!valid_dtype(x_dtype) || !valid_fmt(fmt)) return BRC_ERR_DTYPE;
+  if (n < 0 || history_len < 1) return BRC_ERR_SHAPE;
+  if (margin < -126 || margin > 127) return BRC_ERR_RANGE;
+  if (n > 0 && (!aligned16(x) || !aligned16(codes))) return BRC_ERR_ALIGN;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!use_history) {
+    // no history yet: the reference's current-amax cast, then record its amax
+    int rc = brc_cast_pertensor_fp8(x, x_dtype, n, fmt, codes, scale_out, workspace, stream);
+    if (rc) return rc;
+    brc::delayed::k_history_push<<<1, 32, 0, st>>>(history, history_len, workspace);
+    return check_launch();
+  }
+  return dispatch_dt_fmt<DelayedCast>(x_dtype, fmt, x, n, history, history_len, margin, codes,
+                                      scale_out, workspace, st);
 }

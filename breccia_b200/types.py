@@ -43,7 +43,8 @@ def _check_fp8_format(fmt: str) -> None:  # recipes.py:38-40
 @dataclass(frozen=True)
 class DelayedScaling(ScalingRecipe):
     """Per-tensor FP8 with a TE-style amax history (``recipes.py:43-77``).
-    The cast itself uses the current tensor's amax, as the reference does."""
+    The cast itself uses the current tensor's amax, as the reference does,
+    unless an ``AmaxHistory`` is passed to ``cast`` (extension)."""
 
     name: ClassVar[str] = "delayed"
     fp8_format: str = "E4M3"

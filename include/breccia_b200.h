@@ -97,6 +97,24 @@ int brc_cast_pertensor_fp8(const void* x, int x_dtype, int64_t n, int fmt, uint8
 int brc_cast_pertensor_fp8_noalloc(const void* x, int x_dtype, int64_t n, int fmt,
                                    uint8_t* codes, float* scale_out, void* stream);
 
+/* DelayedScaling with an amax history (extension: the reference's recipe
+ * carries amax_history_len and margin, src/breccia/recipes.py:43-77, but its
+ * cast uses the current amax, cast.py:364-373). `history` is a caller-owned
+ * float32 ring of `history_len` amaxes on the device, most recent first.
+ * use_history = 0: the current-amax cast (brc_cast_pertensor_fp8, bit for bit
+ *   with the reference), then its amax is pushed into the ring.
+ * use_history = 1: the scale is taken from the ring before the tensor is read,
+ *   s = float32(max(max(history), 1e-10) / fmt_max) * 2^margin (a float32
+ *   multiply), and the cast is ONE pass: each element is read once, clipped
+ *   and encoded with s, while the tensor's amax is reduced; that amax is then
+ *   pushed into the ring. Values beyond fmt_max * s saturate as the encoder
+ *   clips them. margin in [-126, 127], else BRC_ERR_RANGE.
+ * scale_out receives the scale used; workspace: one uint32 of device scratch. */
+int brc_cast_pertensor_fp8_delayed(const void* x, int x_dtype, int64_t n, int fmt,
+                                   float* history, int history_len, int margin, int use_history,
+                                   uint8_t* codes, float* scale_out, uint32_t* workspace,
+                                   void* stream);
+
 /* ======================================================= casts: block FP8
  * Float8BlockScaling: one float32 scale per `block_k` run of the last axis.
  * Reference: src/breccia/kernels/reference/cast.py:384-404 (_cast_block_fp8),

@@ -271,6 +271,41 @@ def _dequantize_2d(data, scale, q):
     return out.reshape(dec.shape).astype(np.float32)
 
 
+def cast_delayed_fp8(x, recipe, history, recorded, literal=False):
+    """DelayedScaling with an amax history: a restated oracle for an extension
+    with no reference producer (the reference keeps ``amax_history_len`` and
+    ``margin`` on the recipe, ``recipes.py:43-77``, but its cast uses the
+    current amax, ``cast.py:364-373``).
+
+    ``history``: float32 array, most recent amax first; ``recorded``: how many
+    casts wrote into it. Returns ``(Q, new_history)``. With nothing recorded
+    the result is ``cast_per_tensor_fp8`` (the reference's cast). Otherwise
+    ``s = float32(max(max(history), 1e-10) / fmt_max) * float32(2**margin)``
+    and the codes are ``encode(x / s)`` (float32 division; the encoder clips).
+    The tensor's raw amax is pushed into the history either way."""
+    x = np.asarray(x, dtype=np.float32)
+    history = np.asarray(history, dtype=np.float32)
+    fmt = recipe.fp8_format
+    amax = np.float32(np.max(np.abs(x))) if x.size else np.float32(0.0)
+    if recorded == 0:
+        q = cast_per_tensor_fp8(x, recipe, literal)
+    else:
+        m = np.max(np.abs(history))
+        if np.isnan(m):
+            s = np.float32(np.nan)
+        elif float(m) < 1e-10:
+            s = np.float32(1e-10 / _fmt_max(fmt))
+        else:
+            s = np.float32(np.float32(m) / np.float32(_fmt_max(fmt)))
+        with np.errstate(over="ignore", invalid="ignore"):
+            s = np.float32(s * np.float32(2.0 ** recipe.margin))
+        with np.errstate(divide="ignore", invalid="ignore"):
+            data = _encode_fp8(x / s, fmt, literal)
+        q = Q(data.reshape(x.shape), np.asarray(s, dtype=np.float32), ("per_tensor",), recipe)
+    new_history = np.concatenate([[amax], history[:-1]]).astype(np.float32)
+    return q, new_history
+
+
 def requantize(q: Q, recipe, literal=False) -> Q:
     """``cast.py:339-346``: ``cast(dequantize(st), recipe)``."""
     return cast(dequantize(q), recipe, literal)
