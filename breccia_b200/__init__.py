@@ -17,7 +17,7 @@ from .types import (  # noqa: F401
     Layout, PerTensor, PerBlockK, PerChannel, PerBlockMN,
 )
 from .api import (cast, dequantize, requantize, matmul, linear, gemm_operands,  # noqa: F401
-                  attach_gemm_operands, AmaxHistory)
+                  attach_gemm_operands, AmaxHistory, cast_matmul)
 from . import bridges  # noqa: F401
 from .autograd import cast_ste, cast_ste_clipped  # noqa: F401
 from .plugin import install, uninstall  # noqa: F401

@@ -35,7 +35,7 @@ from . import _lib
 from . import types as T
 
 __all__ = ["cast", "dequantize", "requantize", "matmul", "linear", "gemm_operands",
-           "attach_gemm_operands", "AmaxHistory"]
+           "attach_gemm_operands", "AmaxHistory", "cast_matmul"]
 
 _TORCH_FP8 = {"E4M3": torch.float8_e4m3fn, "E5M2": torch.float8_e5m2}
 _FMT = {"E4M3": _lib.FP8_E4M3, "E5M2": _lib.FP8_E5M2}
@@ -445,6 +445,71 @@ def matmul(a, b, out_dtype=np.float32, *, b_kmajor=False):
     ``a @ b^T``, the layout the block-scaled tensor-core GEMMs consume."""
     from . import gemm
     return gemm.matmul(a, b, _torch_out_dtype(out_dtype), b_kmajor=b_kmajor)
+
+
+def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
+                out_dtype=np.float32, b_kmajor: bool = False, prologue_rows: int = -1):
+    """``matmul(cast(x, recipe), b)`` with the cast fused into the GEMM
+    (extension; the reference casts, then multiplies: ``cast.py:64-92``,
+    ``matmul.py:42-133``). Returns ``(out, a)``: ``a`` is the ScaledTensor
+    ``cast(x, recipe, amax_history=amax_history)`` returns and ``out`` the
+    product ``matmul(a, b, out_dtype, b_kmajor=b_kmajor)`` returns, both bit
+    for bit.
+
+    Fused for a per-tensor recipe (``DelayedScaling`` / ``Float8CurrentScaling``)
+    and a 2-D per-tensor ``b`` with ``K % 128 == 0`` and ``N % 16 == 0``: one
+    GEMM launch whose extra warps encode ``x`` while the tensor cores work, so
+    the activation is not cast in a separate pass first (with an amax history
+    nothing reads ``x`` before the GEMM but the first ``prologue_rows`` rows;
+    ``-1`` = one tile group, 2048). Other inputs take ``cast`` then
+    ``matmul``."""
+    from . import gemm
+    x = _input(x)
+    name = getattr(recipe, "name", None)
+    if amax_history is not None and name != "delayed":
+        raise ValueError("amax_history applies to DelayedScaling only")
+    odt = _torch_out_dtype(out_dtype)
+    K = x.shape[-1] if x.ndim else 0
+    fused = (name in ("delayed", "current") and _is_scaled(b) and
+             getattr(getattr(b, "recipe", None), "name", None) in ("delayed", "current") and
+             b.data.ndim == 2 and b.data.is_cuda and b.data.device == x.device and x.ndim >= 1)
+    if fused:
+        N, Kb = b.data.shape if b_kmajor else tuple(reversed(b.data.shape))
+        fused = Kb == K and K > 0 and K % 128 == 0 and N % 16 == 0
+    if not fused:
+        a = cast(x, recipe, amax_history=amax_history)
+        return matmul(a, b, out_dtype, b_kmajor=b_kmajor), a
+    ST, L = _classes(recipe)
+    fmt = recipe.fp8_format
+    dev = x.device
+    M = x.numel() // K
+    cdt = odt if odt in _OUT_DT else torch.float32
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        w_codes = _codes_u8(b.data) if b_kmajor else gemm._transposed_codes(b)
+        codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
+        scale = torch.empty((), dtype=torch.float32, device=dev)
+        out = torch.empty(x.shape[:-1] + (N,), dtype=cdt, device=dev)
+        ws_bytes = int(_lib.lib().brc_cast_gemm_workspace_bytes(M, K))
+        ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.int32, device=dev)
+        hist, hlen, margin, use = None, 0, 0, 0
+        if amax_history is not None:
+            h = amax_history.history
+            if not (isinstance(h, torch.Tensor) and h.is_cuda and h.dtype == torch.float32 and
+                    h.is_contiguous() and h.device == dev):
+                raise TypeError(
+                    "AmaxHistory.history must be a contiguous float32 tensor on x's device")
+            hist, hlen, margin = h.data_ptr(), h.numel(), int(recipe.margin)
+            use = 1 if amax_history.recorded > 0 else 0
+        _lib.call("brc_cast_gemm_pertensor_fp8", x.data_ptr(), _IN_DT[x.dtype], _FMT[fmt],
+                  w_codes.data_ptr(), _FMT[b.recipe.fp8_format],
+                  b.scale.to(torch.float32).data_ptr(), M, N, K, hist, hlen, margin, use,
+                  codes.data_ptr(), scale.data_ptr(), out.data_ptr(), _OUT_DT[cdt],
+                  ws.data_ptr(), ws_bytes, int(prologue_rows), st)
+    if amax_history is not None:
+        amax_history.recorded += 1
+    a = ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe, layout=L.PerTensor())
+    return (out if cdt == odt else out.to(odt)), a
 
 
 def linear(a, w, out_dtype=torch.bfloat16):

@@ -2071,6 +2071,56 @@ struct DelayedCast {
 };
 }  // namespace
 
+namespace {
+template <int DT, int FMT>
+struct PrefixEncode {
+  static int run(const void* x, int64_t n, const float* scale, uint8_t* codes, uint32_t* amax_ws,
+                 cudaStream_t st) {
+    const int V = In<DT>::kVec;
+    brc::delayed::k_delayed_apply<DT, FMT>
+        <<<grid_for(n / V + 1, 256 * 4), 256, 0, st>>>(x, n, scale, codes, amax_ws);
+    return check_launch();
+  }
+};
+}  // namespace
+
+namespace brc {
+int pertensor_fp8_scale(const void* x, int x_dtype, int64_t n, int fmt, const float* history,
+                        int history_len, int margin, bool from_history, uint32_t* amax_ws,
+                        float* scale_out, cudaStream_t st) {
+  const double fmax = fmt == BRC_FP8_E4M3 ? 448.0 : 57344.0;
+  const float floor_scale = (float)(1e-10 / fmax);
+  if (!from_history) {
+    // the current-amax scale: one amax pass, then the same float32 scale as
+    // the apply kernel (a history of one entry holding the amax, margin 0)
+    int rc = brc_amax_accumulate(x, x_dtype, n, amax_ws, st);
+    if (rc) return rc;
+    history = reinterpret_cast<const float*>(amax_ws);
+    history_len = 1;
+    margin = 0;
+  }
+  if (fmt == BRC_FP8_E4M3)
+    delayed::k_history_scale<BRC_FP8_E4M3><<<1, 32, 0, st>>>(
+        history, history_len, std::ldexp(1.0f, margin), floor_scale, scale_out);
+  else
+    delayed::k_history_scale<BRC_FP8_E5M2><<<1, 32, 0, st>>>(
+        history, history_len, std::ldexp(1.0f, margin), floor_scale, scale_out);
+  return check_launch();
+}
+
+int pertensor_fp8_encode(const void* x, int x_dtype, int64_t n, int fmt, const float* scale,
+                         uint8_t* codes, uint32_t* amax_ws, cudaStream_t st) {
+  if (n <= 0) return BRC_OK;
+  return dispatch_dt_fmt<PrefixEncode>(x_dtype, fmt, x, n, scale, codes, amax_ws, st);
+}
+
+int pertensor_fp8_history_push(float* history, int history_len, const uint32_t* amax_ws,
+                               cudaStream_t st) {
+  delayed::k_history_push<<<1, 32, 0, st>>>(history, history_len, amax_ws);
+  return check_launch();
+}
+}  // namespace brc
+
 extern "C" int brc_cast_pertensor_fp8_delayed(const void* x, int x_dtype, int64_t n, int fmt,
                                               float* history, int history_len, int margin,
                                               int use_history, uint8_t* codes, float* scale_out,

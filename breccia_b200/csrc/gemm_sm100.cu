@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "breccia_b200.h"
+#include "common.cuh"
 #include "launch.h"
 #include "sm100.cuh"
 
@@ -125,6 +126,16 @@ struct Params {
   const float* bsb;       // (ceil(N/128), K/128): one scale per 128x128 tile of B
   int bs_ld;              // K / 128
   int group_m;            // row blocks per tile group (tile order)
+  // fused activation cast (k_gemm_pair with CAST != 0): A's source tensor,
+  // the codes the casters write (tmap_a reads them), the amax they reduce,
+  // the cast-unit queue and the per-(256-row block, K chunk) ready counters
+  const void* x;
+  uint8_t* a_codes;
+  uint32_t* amax_bits;
+  uint32_t* cast_next;
+  uint32_t* cast_ready;
+  int first_rows;         // rows [0, first_rows) were encoded before the launch
+  int kchunks;            // ceil(K / kCastChunk)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
@@ -527,8 +538,79 @@ struct PairCfg {
                 "TMEM overflow");
 };
 
-template <int KIND, int AFMT, int BFMT, int OUT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
+// ------------------------------------------------------------ fused activation cast
+// Per-tensor FP8 GEMM whose A operand is cast inside the kernel (template
+// argument CAST = 1 + the activation's BRC_DTYPE_*; 0 = no cast). Encoding A in each tile's producer would repeat the
+// encode once per N tile (32 times at N = 8192) at about 7 instructions per
+// element, more than the issue slots a 256 x 256 x 128 FP8 stage leaves.
+// Instead kCastWarps extra warps per CTA encode A once, into the codes
+// tensor, in the order the tiles consume it: tile group by tile group (the
+// kGroupM row blocks of the tile order), K chunk by K chunk, 32-row slab by
+// slab. Units are claimed from a global queue, so no caster waits on anyone
+// and every unit is taken by whichever CTA is running. After a slab's codes
+// are stored the warp adds one to the ready counter of its (256-row block, K
+// chunk); the producer waits (bounded) for a block's full count before its
+// first TMA load of that chunk. Rows [0, first_rows) are encoded by a cast
+// kernel before the launch, so the first tiles start at once; the rest is
+// encoded while the tensor cores work on earlier groups.
+constexpr int kCastWarps = 2;
+constexpr int kCastChunk = 1024;  // K elements (code bytes) per ready counter
+constexpr int kCastSlab = 32;     // rows per cast unit
+constexpr int kKbPerChunk = kCastChunk / BKB;
+static_assert(P_BM % kCastSlab == 0, "a slab must not straddle a row block");
+template <int KIND, int CAST>
+constexpr int kThreadsP = kThreadsG<KIND> + (CAST != 0 ? 32 * kCastWarps : 0);
+
+// Unit u -> (first row of its slab, K chunk); false past the last unit.
+__device__ __forceinline__ bool cast_unit(int u, const Params& p, int& row0, int& kc) {
+  const int G = p.group_m * P_BM;
+  for (int g0 = (p.first_rows / G) * G; g0 < p.M; g0 += G) {
+    const int r0 = max(g0, p.first_rows), r1 = min(g0 + G, p.M);
+    const int slabs = (r1 - r0 + kCastSlab - 1) / kCastSlab;
+    const int n = slabs * p.kchunks;
+    if (u < n) {
+      kc = u / slabs;
+      row0 = r0 + kCastSlab * (u - kc * slabs);
+      return true;
+    }
+    u -= n;
+  }
+  return false;
+}
+
+// Encode one 16-byte vector of A with the per-tensor scale s (r = RN(1/s)):
+// the encoders and division of the per-tensor cast kernels, so the codes are
+// theirs bit for bit. A vector holding NaN, or a non-finite scale, takes the
+// per-element path (NaN -> the NaN code).
+template <int XDT, int FMT>
+__device__ __forceinline__ void cast_vector(const uint4 v, float s, float r, bool fast,
+                                            float& m, uint8_t* dst) {
+  constexpr int V = In<XDT>::kVec;
+  const float vmax = vec_absmax<XDT>(v);
+  m = fmax_nan(m, vmax);
+  float f[V];
+  unpack<XDT>(v, f);
+  uint32_t w[V / 4];
+  if (fast && !isnan(vmax)) {
+#pragma unroll
+    for (int j = 0; j < V / 4; ++j)
+      w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
+                           div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+  } else {
+#pragma unroll
+    for (int j = 0; j < V / 4; ++j) {
+      uint32_t c = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c |= enc1_fp8<FMT>(div_ieee(f[4 * j + i], s)) << (8 * i);
+      w[j] = c;
+    }
+  }
+  if constexpr (V == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  else *reinterpret_cast<uint32_t*>(dst) = w[0];
+}
+
+template <int KIND, int AFMT, int BFMT, int OUT, int CAST = 0>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST>, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_sfa,
@@ -631,6 +713,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
                              (2 * nb) * (int)p.sf_col_tiles + kcol, sb);
             tma_load_2d_pair(smem + C::kSfB + stage * C::kSfb + C::kSfb / 2, &tmap_sfb, 0,
                              (2 * nb + 1) * (int)p.sf_col_tiles + kcol, sb);
+          }
+          if constexpr (CAST != 0) {
+            // A's codes of this K chunk: cast before the launch, or wait for
+            // every slab of this row block
+            if (kb % kKbPerChunk == 0 && mb * P_BM >= p.first_rows) {
+              const uint32_t slabs = (min(P_BM, p.M - mb * P_BM) + kCastSlab - 1) / kCastSlab;
+              if (!counter_wait(p.cast_ready + (size_t)mb * p.kchunks + kb / kKbPerChunk, slabs,
+                                abort_flag, p.status, 1u)) {
+                ok = false;
+                break;
+              }
+              fence_proxy_async_global();
+            }
           }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
           const uint32_t fb = full_leader + 8u * stage;
@@ -814,6 +909,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG<KIND>, 1)
         }
       }
       __syncwarp();
+    }
+  } else if (CAST != 0 && warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------------------ activation casters
+    if constexpr (CAST != 0) {
+      constexpr int XDT = CAST - 1;
+      constexpr int V = In<XDT>::kVec;
+      constexpr int PER = kCastChunk / V / 32;  // vectors per lane per row of a chunk
+      constexpr int R = 16 / PER;               // rows per batch: 16 loads in flight per lane
+      constexpr size_t kEsz = XDT == BRC_DTYPE_F32 ? 4 : 2;
+      const float s = *p.a_scale;
+      const bool fast = isfinite(s) && s > 0.f;
+      const float rcp = __frcp_rn(s);
+      const uint64_t pol = l2_evict_first_policy();  // each input line is read once
+      const char* xb = static_cast<const char*>(p.x);
+      float m = 0.f;
+      while (!*abort_flag) {
+        uint32_t u = 0;
+        if (lane == 0) u = atomicAdd(p.cast_next, 1u);
+        u = __shfl_sync(0xffffffffu, u, 0);
+        int row0, kc;
+        if (!cast_unit((int)u, p, row0, kc)) break;
+        const int k0 = kc * kCastChunk;
+        const int nv = min(kCastChunk, p.K - k0) / V;
+        const int rows = min(kCastSlab, p.M - row0);
+        for (int r0 = 0; r0 < rows; r0 += R) {
+          uint4 v[R][PER];
+#pragma unroll
+          for (int h = 0; h < R; ++h)
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+              const int j = lane + 32 * q;
+              v[h][q] = make_uint4(0u, 0u, 0u, 0u);
+              if (r0 + h < rows && j < nv)
+                v[h][q] = ldg16_last_use(
+                    xb + ((size_t)(row0 + r0 + h) * p.K + k0 + (size_t)j * V) * kEsz, pol);
+            }
+#pragma unroll
+          for (int h = 0; h < R; ++h)
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+              const int j = lane + 32 * q;
+              if (r0 + h < rows && j < nv)
+                cast_vector<XDT, AFMT>(v[h][q], s, rcp, fast, m,
+                                       p.a_codes + (size_t)(row0 + r0 + h) * p.K + k0 +
+                                           (size_t)j * V);
+            }
+        }
+        // publish the slab: every lane's stores, then one count
+        fence_proxy_async_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0)
+          red_release_gpu_add(p.cast_ready + (size_t)(row0 / P_BM) * p.kchunks + kc, 1u);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0 && __float_as_uint(m) != 0u) atomicMax(p.amax_bits, __float_as_uint(m));
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -1157,10 +1309,10 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
   return check_launch();
 }
 
-template <int KIND, int AFMT, int BFMT, int OUT>
+template <int KIND, int AFMT, int BFMT, int OUT, int CAST = 0>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
                 const CUtensorMap& tsb, const Params& p, cudaStream_t st) {
-  auto kern = k_gemm_pair<KIND, AFMT, BFMT, OUT>;
+  auto kern = k_gemm_pair<KIND, AFMT, BFMT, OUT, CAST>;
   const int smem = (int)PairCfg<KIND>::kAlloc;
   static bool configured[64] = {};
   int dev = 0;
@@ -1174,7 +1326,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int tiles = p.num_m * p.num_n;
   const int pairs = sm_count() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreadsG<KIND>, smem, st>>>(ta, tb, tsa, tsb, p);
+  kern<<<grid, kThreadsP<KIND, CAST>, smem, st>>>(ta, tb, tsa, tsb, p);
   return check_launch();
 }
 
@@ -1187,6 +1339,34 @@ int launch_pair_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb,
   if (out_dtype == BRC_DTYPE_BF16)
     return launch_pair<KIND, AFMT, BFMT, BRC_DTYPE_BF16>(ta, tb, tsa, tsb, p, st);
   return launch_pair<KIND, AFMT, BFMT, BRC_DTYPE_F16>(ta, tb, tsa, tsb, p, st);
+}
+
+// Fused-cast pair kernel for (activation dtype, A / B formats, output dtype).
+template <int CAST, int AFMT, int BFMT>
+int launch_cast_pair_out(int out_dtype, const CUtensorMap& ta, const CUtensorMap& tb,
+                         const Params& p, cudaStream_t st) {
+  if (out_dtype == BRC_DTYPE_F32)
+    return launch_pair<kPerTensor, AFMT, BFMT, BRC_DTYPE_F32, CAST>(ta, tb, ta, tb, p, st);
+  if (out_dtype == BRC_DTYPE_BF16)
+    return launch_pair<kPerTensor, AFMT, BFMT, BRC_DTYPE_BF16, CAST>(ta, tb, ta, tb, p, st);
+  return launch_pair<kPerTensor, AFMT, BFMT, BRC_DTYPE_F16, CAST>(ta, tb, ta, tb, p, st);
+}
+template <int CAST>
+int launch_cast_pair_fmt(int a_fmt, int b_fmt, int out_dtype, const CUtensorMap& ta,
+                         const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  if (a_fmt == BRC_FP8_E4M3 && b_fmt == BRC_FP8_E4M3)
+    return launch_cast_pair_out<CAST, 0, 0>(out_dtype, ta, tb, p, st);
+  if (a_fmt == BRC_FP8_E4M3) return launch_cast_pair_out<CAST, 0, 1>(out_dtype, ta, tb, p, st);
+  if (b_fmt == BRC_FP8_E4M3) return launch_cast_pair_out<CAST, 1, 0>(out_dtype, ta, tb, p, st);
+  return launch_cast_pair_out<CAST, 1, 1>(out_dtype, ta, tb, p, st);
+}
+int launch_cast_pair(int x_dtype, int a_fmt, int b_fmt, int out_dtype, const CUtensorMap& ta,
+                     const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  if (x_dtype == BRC_DTYPE_BF16)
+    return launch_cast_pair_fmt<1 + BRC_DTYPE_BF16>(a_fmt, b_fmt, out_dtype, ta, tb, p, st);
+  if (x_dtype == BRC_DTYPE_F16)
+    return launch_cast_pair_fmt<1 + BRC_DTYPE_F16>(a_fmt, b_fmt, out_dtype, ta, tb, p, st);
+  return launch_cast_pair_fmt<1 + BRC_DTYPE_F32>(a_fmt, b_fmt, out_dtype, ta, tb, p, st);
 }
 
 // Scale atoms (512 bytes each, row group-major) as a 2-D tensor of rows of
@@ -1404,6 +1584,77 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
   if (a_fmt == BRC_FP8_E4M3) return launch_out<kPerTensor, 0, 1>(d_dtype, ta, tb, p, st);
   if (b_fmt == BRC_FP8_E4M3) return launch_out<kPerTensor, 1, 0>(d_dtype, ta, tb, p, st);
   return launch_out<kPerTensor, 1, 1>(d_dtype, ta, tb, p, st);
+}
+
+int64_t brc_cast_gemm_workspace_bytes(int M, int K) {
+  if (M < 0 || K < 0) return -1;
+  const int64_t mblocks = (M + P_BM - 1) / P_BM, kchunks = (K + kCastChunk - 1) / kCastChunk;
+  return 16 + 4 * mblocks * kchunks;
+}
+
+int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uint8_t* b,
+                                int b_fmt, const float* b_scale, int M, int N, int K,
+                                float* history, int history_len, int margin, int use_history,
+                                uint8_t* a_codes, float* a_scale_out, void* d, int d_dtype,
+                                void* workspace, int64_t workspace_bytes, int prologue_rows,
+                                void* stream) {
+  if (!a_codes || !a_scale_out || !workspace || !b_scale) return BRC_ERR_NULL;
+  int rc = check_common(x, b, d, M, N, K, d_dtype, BKB);
+  if (rc) return rc;
+  if (x_dtype != BRC_DTYPE_F32 && x_dtype != BRC_DTYPE_BF16 && x_dtype != BRC_DTYPE_F16)
+    return BRC_ERR_DTYPE;
+  if ((a_fmt != BRC_FP8_E4M3 && a_fmt != BRC_FP8_E5M2) ||
+      (b_fmt != BRC_FP8_E4M3 && b_fmt != BRC_FP8_E5M2))
+    return BRC_ERR_DTYPE;
+  if (reinterpret_cast<uintptr_t>(a_codes) & 15) return BRC_ERR_ALIGN;
+  if (history && history_len < 1) return BRC_ERR_SHAPE;
+  if (margin < -126 || margin > 127) return BRC_ERR_RANGE;
+  if (workspace_bytes < brc_cast_gemm_workspace_bytes(M, K)) return BRC_ERR_SHAPE;
+  if (K == 0 && M > 0 && N > 0) return BRC_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = (int64_t)M * K;
+  uint32_t* ws = static_cast<uint32_t*>(workspace);
+  if ((rc = check_cuda(cudaMemsetAsync(ws, 0, (size_t)brc_cast_gemm_workspace_bytes(M, K), st))))
+    return rc;
+  // 1. the scale: from the history, or from the amax of the whole tensor
+  const bool from_history = history && use_history;
+  if ((rc = pertensor_fp8_scale(x, x_dtype, n, a_fmt, history, history_len, margin, from_history,
+                                ws, a_scale_out, st)))
+    return rc;
+  // 2. the first tile group's rows, before the GEMM (all of A when there is
+  //    no GEMM to overlap with)
+  int first = M;
+  if (N > 0) {
+    const int group_rows = (kGroupM / 2) * P_BM;
+    first = prologue_rows < 0 ? group_rows : prologue_rows / P_BM * P_BM;
+    if (first > M) first = M;
+  }
+  if ((rc = pertensor_fp8_encode(x, x_dtype, (int64_t)first * K, a_fmt, a_scale_out, a_codes, ws,
+                                 st)))
+    return rc;
+  // 3. the GEMM, its casters encoding rows [first, M)
+  if (N > 0 && M > 0) {
+    CUtensorMap ta, tb;
+    if ((rc = make_tmap(&ta, a_codes, M, K, 128))) return rc;
+    if ((rc = make_tmap(&tb, b, N, K, 128))) return rc;
+    Params p = base_params(M, N, K, BKB, d);
+    to_pair_params(p);
+    p.a_scale = a_scale_out;
+    p.b_scale = b_scale;
+    p.status = status_word();
+    p.x = x;
+    p.a_codes = a_codes;
+    p.amax_bits = ws;
+    p.cast_next = ws + 1;
+    p.cast_ready = ws + 4;
+    p.first_rows = first;
+    p.kchunks = (K + kCastChunk - 1) / kCastChunk;
+    rc = launch_cast_pair(x_dtype, a_fmt, b_fmt, d_dtype, ta, tb, p, st);
+    if (rc) return rc;
+  }
+  // 4. the history records this tensor's amax
+  if (history) return pertensor_fp8_history_push(history, history_len, ws, st);
+  return BRC_OK;
 }
 
 int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,

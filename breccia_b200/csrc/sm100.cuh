@@ -105,6 +105,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ----------------------------------------------------------------- ready counters
+// Data written with ordinary stores by warps of other CTAs and then loaded
+// by this CTA's TMA: the writers publish with a release add on a counter in
+// global memory; the TMA-issuing thread observes it with acquire loads and
+// then a proxy fence, which orders its generic-proxy view before its later
+// async-proxy (TMA) reads of the same bytes.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Wait until *counter >= target, bounded like mbar_wait (same status code and
+// abort-flag contract). The counter's writers never wait on this CTA.
+__device__ __forceinline__ bool counter_wait(const uint32_t* counter, uint32_t target,
+                                             volatile uint32_t* abort_flag, uint32_t* status,
+                                             uint32_t code) {
+  if (ld_acquire_gpu(counter) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(200);
+    if (ld_acquire_gpu(counter) >= target) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1u;
+      if (status) atomicOr(status, code);
+      return false;
+    }
+  }
+}
+
 // ----------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -282,6 +282,25 @@ int brc_requant_nvfp4_to_mxfp8(const uint8_t* codes, const uint8_t* scales, int6
 int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
                            int b_fmt, const float* a_scale, const float* b_scale, void* d,
                            int d_dtype, void* stream);
+/* Fused activation cast + per-tensor FP8 GEMM (extension: the reference
+ * casts, then multiplies -- cast.py:364-373 then matmul.py:42-133).
+ * x (M, K) float32 / bfloat16 / float16 is cast to a_fmt codes and
+ *   D = (A_codes @ B_codes^T) * a_scale * b_scale
+ * in one GEMM launch whose extra warps encode A while the tensor cores run;
+ * only the first tile group's rows (prologue_rows, < 0 = 2048) are encoded
+ * before it. Outputs equal brc_cast_pertensor_fp8 (history == NULL, or
+ * use_history == 0) or brc_cast_pertensor_fp8_delayed (history, use_history)
+ * followed by brc_gemm_fp8_pertensor, bit for bit: a_codes / a_scale_out are
+ * the cast's, d the GEMM's; with a history its ring receives x's amax.
+ * workspace: device scratch of brc_cast_gemm_workspace_bytes(M, K) bytes
+ * (zeroed here). K % 128 == 0, N % 16 == 0, 16-byte aligned pointers. */
+int64_t brc_cast_gemm_workspace_bytes(int M, int K);
+int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uint8_t* b,
+                                int b_fmt, const float* b_scale, int M, int N, int K,
+                                float* history, int history_len, int margin, int use_history,
+                                uint8_t* a_codes, float* a_scale_out, void* d, int d_dtype,
+                                void* workspace, int64_t workspace_bytes, int prologue_rows,
+                                void* stream);
 /* MXFP8: scales in the tcgen05 layout written by brc_cast_mxfp8 (scales_mma)
  * for A (M rows) and B (N rows). K % 128 == 0. */
 int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,
