@@ -917,7 +917,32 @@ def per_recipe(peaks, src):
         "ms": ms, "TFLOP/s": FLOPS / (ms * 1e-3) / 1e12,
         "what": "C2 step with the activation cast from its amax history (one pass) instead of "
                 "the current amax (two passes); same GEMM"}
-    del A, Wt, hist
+    # The activation cast fused into the GEMM (cast_matmul: two warps per CTA
+    # encode A in tile-group order while the tensor cores run) against the
+    # cast followed by the GEMM; the weight is cast beforehand. Interleaved,
+    # median of three.
+    wc = bb.cast(Wt, rc)
+    variants = {
+        "unfused_current": lambda: bb.linear(bb.cast(A, rc), wc, out_dtype=torch.bfloat16),
+        "fused_current": lambda: bb.cast_matmul(A, wc, rc, out_dtype=torch.bfloat16,
+                                                b_kmajor=True, fused=True),
+        "unfused_delayed": lambda: bb.linear(bb.cast(A, rd, amax_history=hist), wc,
+                                             out_dtype=torch.bfloat16),
+        "fused_delayed": lambda: bb.cast_matmul(A, wc, rd, amax_history=hist,
+                                                out_dtype=torch.bfloat16, b_kmajor=True,
+                                                fused=True),
+    }
+    times = {k: [] for k in variants}
+    for _ in range(3):
+        for k, f in variants.items():
+            times[k].append(_time_graph(f, reps=8))
+    entry = {"what": "C2 activation cast + GEMM (weight cast beforehand): the cast fused into the "
+                     "GEMM launch vs a separate cast kernel; same codes and product bit for bit"}
+    for k, v in times.items():
+        ms = statistics.median(v)
+        entry[k] = {"ms": ms, "TFLOP/s": FLOPS / (ms * 1e-3) / 1e12}
+    res["c2_cast_A_gemm_fused_vs_unfused"] = entry
+    del A, Wt, hist, wc, variants
 
     # C3 MXFP8: A bf16 (8192, 8192), W^T bf16 (28672, 8192); GEMM 8192 x 28672 x 8192
     r = bb.MXFP8BlockScaling()

@@ -447,22 +447,32 @@ def matmul(a, b, out_dtype=np.float32, *, b_kmajor=False):
     return gemm.matmul(a, b, _torch_out_dtype(out_dtype), b_kmajor=b_kmajor)
 
 
+# Narrowest GEMM (output columns) for which cast_matmul picks the fused
+# kernel by itself: C2 (16384 x 8192 x 8192) measured fused 0.822 vs 0.835 ms
+# (delayed) and 0.864 vs 0.866 ms (current); at N = 4096 the fused launch took
+# 0.52-0.58 ms against 0.44-0.47 ms for cast then GEMM.
+_FUSED_MIN_N = 8192
+
+
 def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
-                out_dtype=np.float32, b_kmajor: bool = False, prologue_rows: int = -1):
+                out_dtype=np.float32, b_kmajor: bool = False, fused: Optional[bool] = None,
+                prologue_rows: int = -1):
     """``matmul(cast(x, recipe), b)`` with the cast fused into the GEMM
     (extension; the reference casts, then multiplies: ``cast.py:64-92``,
     ``matmul.py:42-133``). Returns ``(out, a)``: ``a`` is the ScaledTensor
     ``cast(x, recipe, amax_history=amax_history)`` returns and ``out`` the
     product ``matmul(a, b, out_dtype, b_kmajor=b_kmajor)`` returns, both bit
-    for bit.
+    for bit, whichever way it runs.
 
-    Fused for a per-tensor recipe (``DelayedScaling`` / ``Float8CurrentScaling``)
-    and a 2-D per-tensor ``b`` with ``K % 128 == 0`` and ``N % 16 == 0``: one
-    GEMM launch whose extra warps encode ``x`` while the tensor cores work, so
-    the activation is not cast in a separate pass first (with an amax history
-    nothing reads ``x`` before the GEMM but the first ``prologue_rows`` rows;
-    ``-1`` = one tile group, 2048). Other inputs take ``cast`` then
-    ``matmul``."""
+    The fused kernel takes a per-tensor recipe (``DelayedScaling`` /
+    ``Float8CurrentScaling``) and a 2-D per-tensor ``b`` with ``K % 128 == 0``
+    and ``N % 16 == 0``: one GEMM launch whose extra warps encode ``x`` while
+    the tensor cores work (only the first ``prologue_rows`` rows, ``-1`` = one
+    tile group of 2048, are encoded before it). ``fused=None`` uses it where
+    it measured no slower than the separate cast on B200: ``N >= 8192`` (each
+    activation tile feeds at least 32 output tiles); below that the in-kernel
+    encode cannot keep up and ``cast`` then ``matmul`` runs. ``True`` / ``False``
+    force either way (``True`` still needs the shape conditions)."""
     from . import gemm
     x = _input(x)
     name = getattr(recipe, "name", None)
@@ -470,13 +480,15 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
         raise ValueError("amax_history applies to DelayedScaling only")
     odt = _torch_out_dtype(out_dtype)
     K = x.shape[-1] if x.ndim else 0
-    fused = (name in ("delayed", "current") and _is_scaled(b) and
+    ok = (name in ("delayed", "current") and _is_scaled(b) and
              getattr(getattr(b, "recipe", None), "name", None) in ("delayed", "current") and
              b.data.ndim == 2 and b.data.is_cuda and b.data.device == x.device and x.ndim >= 1)
-    if fused:
+    if ok:
         N, Kb = b.data.shape if b_kmajor else tuple(reversed(b.data.shape))
-        fused = Kb == K and K > 0 and K % 128 == 0 and N % 16 == 0
-    if not fused:
+        ok = Kb == K and K > 0 and K % 128 == 0 and N % 16 == 0
+        if ok and fused is None:
+            ok = N >= _FUSED_MIN_N
+    if not ok or fused is False:
         a = cast(x, recipe, amax_history=amax_history)
         return matmul(a, b, out_dtype, b_kmajor=b_kmajor), a
     ST, L = _classes(recipe)

@@ -134,6 +134,7 @@ struct Params {
   uint32_t* amax_bits;
   uint32_t* cast_next;
   uint32_t* cast_ready;
+  uint32_t* gemm_group;   // the highest tile group any producer has reached
   int first_rows;         // rows [0, first_rows) were encoded before the launch
   int kchunks;            // ceil(K / kCastChunk)
 };
@@ -553,7 +554,16 @@ struct PairCfg {
 // first TMA load of that chunk. Rows [0, first_rows) are encoded by a cast
 // kernel before the launch, so the first tiles start at once; the rest is
 // encoded while the tensor cores work on earlier groups.
+// The casters keep at most kCastLead groups ahead of the furthest producer:
+// running ahead through the whole tensor at launch, their reads and code
+// writes crowded the first groups' operand traffic out of HBM and L2 and
+// slowed the GEMM by 6-9%. Held back, their traffic spreads over the GEMM
+// and a group's codes are still in L2 when its tiles load them. The hold is
+// a bounded pause, not a dependency: a unit a producer waits for is never
+// held (a producer publishes its group before it waits).
 constexpr int kCastWarps = 2;
+constexpr uint32_t kCastLead = 1;
+constexpr uint64_t kCastHoldNs = 20000000ull;  // 20 ms, then cast regardless
 constexpr int kCastChunk = 1024;  // K elements (code bytes) per ready counter
 constexpr int kCastSlab = 32;     // rows per cast unit
 constexpr int kKbPerChunk = kCastChunk / BKB;
@@ -592,10 +602,14 @@ __device__ __forceinline__ void cast_vector(const uint4 v, float s, float r, boo
   unpack<XDT>(v, f);
   uint32_t w[V / 4];
   if (fast && !isnan(vmax)) {
+    // packed-pair forms (same roundings, half the FMA-pipe instructions):
+    // these warps share their SM's issue slots with the GEMM's
 #pragma unroll
-    for (int j = 0; j < V / 4; ++j)
-      w[j] = enc4_fp8<FMT>(div_by(f[4 * j], s, r), div_by(f[4 * j + 1], s, r),
-                           div_by(f[4 * j + 2], s, r), div_by(f[4 * j + 3], s, r));
+    for (int j = 0; j < V / 4; ++j) {
+      float q[4];
+      div4(f + 4 * j, s, r, q);
+      w[j] = enc4p_fp8<FMT>(q[0], q[1], q[2], q[3]);
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < V / 4; ++j) {
@@ -686,6 +700,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, issued_parity = 0;  // per-stage bits for the drain
+      uint32_t published = 0;                  // 1 + the group last published
+      uint64_t ready_lo = 0ull, ready_hi = 0ull;  // row blocks < 128 whose codes are all ready
+      auto seen_ready = [&](int mb) {
+        return mb < 128 && (((mb < 64 ? ready_lo : ready_hi) >> (mb & 63)) & 1ull);
+      };
       bool ok = true;
       for (int tile = cluster; ok && tile < num_tiles; tile += nclusters) {
         int mb, nb;
@@ -693,6 +712,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST
         // scale atoms (2-D copies of 512-byte rows; rows past the operand's
         // end read as zeros): this CTA's 128 A rows and the tile's 256 B^T rows
         const int a_atom = 2 * mb + (int)rank;
+        if constexpr (CAST != 0) {
+          // publish this tile's group before waiting on any of its codes
+          const uint32_t grp = (uint32_t)(mb / p.group_m);
+          if (grp + 1 > published) {
+            atomicMax(p.gemm_group, grp);
+            published = grp + 1;
+          }
+        }
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, 1u)) {
             ok = false;
@@ -716,8 +743,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST
           }
           if constexpr (CAST != 0) {
             // A's codes of this K chunk: cast before the launch, or wait for
-            // every slab of this row block
-            if (kb % kKbPerChunk == 0 && mb * P_BM >= p.first_rows) {
+            // every slab of this row block (once per row block and producer:
+            // a block whose chunks were all seen ready is remembered)
+            if (kb % kKbPerChunk == 0 && mb * P_BM >= p.first_rows && !seen_ready(mb)) {
               const uint32_t slabs = (min(P_BM, p.M - mb * P_BM) + kCastSlab - 1) / kCastSlab;
               if (!counter_wait(p.cast_ready + (size_t)mb * p.kchunks + kb / kKbPerChunk, slabs,
                                 abort_flag, p.status, 1u)) {
@@ -739,6 +767,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST
             stage = 0;
             phase ^= 1u;
           }
+        }
+        if constexpr (CAST != 0) {
+          if (ok && mb < 64) ready_lo |= 1ull << mb;
+          else if (ok && mb < 128) ready_hi |= 1ull << (mb - 64);
         }
       }
       if (!ok && rank == 0) {
@@ -930,6 +962,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP<KIND, CAST
         u = __shfl_sync(0xffffffffu, u, 0);
         int row0, kc;
         if (!cast_unit((int)u, p, row0, kc)) break;
+        if (lane == 0) {
+          const uint32_t grp = (uint32_t)(row0 / (p.group_m * P_BM));
+          if (grp > ld_acquire_gpu(p.gemm_group) + kCastLead) {
+            const uint64_t t0 = globaltimer();
+            do {
+              __nanosleep(2000);
+            } while (grp > ld_acquire_gpu(p.gemm_group) + kCastLead && !*abort_flag &&
+                     globaltimer() - t0 < kCastHoldNs);
+          }
+        }
+        __syncwarp();
         const int k0 = kc * kCastChunk;
         const int nv = min(kCastChunk, p.K - k0) / V;
         const int rows = min(kCastSlab, p.M - row0);
@@ -1646,6 +1689,7 @@ int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uin
     p.a_codes = a_codes;
     p.amax_bits = ws;
     p.cast_next = ws + 1;
+    p.gemm_group = ws + 2;
     p.cast_ready = ws + 4;
     p.first_rows = first;
     p.kchunks = (K + kCastChunk - 1) / kCastChunk;

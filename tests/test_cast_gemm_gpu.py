@@ -47,6 +47,7 @@ def _weight(N, K, fmt="E4M3", seed=1, kmajor=True):
 
 def _check_against_unfused(x, w, recipe, out_dtype=torch.float32, kmajor=True, **kw):
     import breccia_b200 as bb
+    kw.setdefault("fused", True)
     out, a = bb.cast_matmul(x, w, recipe, out_dtype=out_dtype, b_kmajor=kmajor, **kw)
     a_ref = bb.cast(x, recipe)
     out_ref = bb.matmul(a_ref, w, out_dtype, b_kmajor=kmajor)
@@ -78,7 +79,7 @@ def test_fused_ragged_shapes(M, N, K):
     g = torch.Generator().manual_seed(M + N + K)
     x = (torch.randn(M, K, generator=g) * 0.7).to(torch.bfloat16).cuda()
     w = _weight(N, K, seed=K)
-    _check_against_unfused(x, w, bb.Float8CurrentScaling(), prologue_rows=0)
+    _check_against_unfused(x, w, bb.Float8CurrentScaling(), fused=True, prologue_rows=0)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
@@ -90,7 +91,7 @@ def test_fused_dtypes_formats(dtype, afmt, wfmt):
     M, N, K = 640, 768, 1280
     x = (torch.randn(M, K, generator=g) * 5).to(dtype).cuda()
     w = _weight(N, K, fmt=wfmt)
-    _check_against_unfused(x, w, bb.Float8CurrentScaling(fp8_format=afmt), prologue_rows=0)
+    _check_against_unfused(x, w, bb.Float8CurrentScaling(fp8_format=afmt), fused=True, prologue_rows=0)
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
@@ -100,9 +101,9 @@ def test_fused_out_dtypes_and_orientation(out_dtype):
     M, N, K = 512, 1024, 1024
     x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
     _check_against_unfused(x, _weight(N, K), bb.Float8CurrentScaling(), out_dtype=out_dtype,
-                           prologue_rows=0)
+                           fused=True, prologue_rows=0)
     _check_against_unfused(x, _weight(N, K, kmajor=False), bb.Float8CurrentScaling(),
-                           out_dtype=out_dtype, kmajor=False, prologue_rows=0)
+                           out_dtype=out_dtype, kmajor=False, fused=True, prologue_rows=0)
 
 
 def test_fused_codes_match_oracle():
@@ -117,7 +118,7 @@ def test_fused_codes_match_oracle():
     xb = x.to(torch.bfloat16)
     w = _weight(N, K)
     r = bb.Float8CurrentScaling()
-    out, a = bb.cast_matmul(xb.cuda(), w, r, prologue_rows=0)
+    out, a = bb.cast_matmul(xb.cuda(), w, r, b_kmajor=True, fused=True, prologue_rows=0)
     q = ocast.cast_per_tensor_fp8(xb.float().numpy(), r)
     torch.cuda.synchronize()
     assert same_bits(_u8(a.data), q.data)
@@ -137,16 +138,16 @@ def test_fused_special_values():
     w = _weight(N, K)
     r = bb.Float8CurrentScaling()
     zeros = torch.zeros(M, K, dtype=torch.bfloat16, device="cuda")
-    _check_against_unfused(zeros, w, r, prologue_rows=0)
+    _check_against_unfused(zeros, w, r, fused=True, prologue_rows=0)
     x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
     x[300, 17] = float("nan")    # current scaling: the scale becomes NaN
-    out, a = bb.cast_matmul(x, w, r, prologue_rows=0)
+    out, a = bb.cast_matmul(x, w, r, b_kmajor=True, fused=True, prologue_rows=0)
     a_ref = bb.cast(x, r)
     torch.cuda.synchronize()
     assert same_bits(_u8(a.data), _u8(a_ref.data))
     assert torch.isnan(a.scale).item()
     x[300, 17] = float("inf")
-    _, a = bb.cast_matmul(x, w, r, prologue_rows=0)
+    _, a = bb.cast_matmul(x, w, r, b_kmajor=True, fused=True, prologue_rows=0)
     assert same_bits(_u8(a.data), _u8(bb.cast(x, r).data))
 
 
@@ -169,7 +170,8 @@ def test_fused_history_sequence(dtype, fmt, margin):
             # encoded by the in-kernel casters with a finite scale (the NaN
             # code), then pushed: the following calls' scale is NaN
             x[1000, 3] = float("nan")
-        out, a = bb.cast_matmul(x.cuda(), w, r, amax_history=h, prologue_rows=256)
+        out, a = bb.cast_matmul(x.cuda(), w, r, amax_history=h, b_kmajor=True, fused=True,
+                                prologue_rows=256)
         a2 = bb.cast(x.cuda(), r, amax_history=h2)
         out2 = bb.matmul(a2, w, np.float32, b_kmajor=True)
         q, hist = ocast.cast_delayed_fp8(x.float().numpy(), r, hist, recorded)
@@ -203,7 +205,7 @@ def test_fused_large_many_units():
     x = (torch.randn(M, K, generator=g) * 4).to(torch.bfloat16).cuda()
     w = _weight(N, K)
     _check_against_unfused(x, w, bb.Float8CurrentScaling(), out_dtype=torch.bfloat16,
-                           prologue_rows=0)
+                           fused=True, prologue_rows=0)
 
 
 def test_fused_arguments():
