@@ -145,6 +145,17 @@ def _mma_scale_shape(rows: int, scale_cols: int):
     return (((rows + 127) // 128) * ((scale_cols + 3) // 4) * 512,)
 
 
+def _mma_scale_buffer(rows: int, scale_cols: int, dev):
+    """Scale atoms for the tcgen05 GEMMs (128 rows x 4 scale columns per
+    512-byte atom). The cast writes one byte per (row, scale column); atom
+    bytes past the last row or column must read as zero, so only a ragged
+    shape needs the buffer cleared first (a separate fill kernel)."""
+    shape = _mma_scale_shape(rows, scale_cols)
+    if rows % 128 == 0 and scale_cols % 4 == 0:
+        return torch.empty(shape, dtype=torch.uint8, device=dev)
+    return torch.zeros(shape, dtype=torch.uint8, device=dev)
+
+
 # ------------------------------------------------------------------- cast
 
 
@@ -284,7 +295,7 @@ def _cast_mxfp8(x, recipe, ST, L, st):
     rows = x.numel() // K if K else 0
     codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
     scale = torch.empty(x.shape[:-1] + (K // 32,), dtype=torch.uint8, device=x.device)
-    sf_mma = torch.zeros(_mma_scale_shape(rows, K // 32), dtype=torch.uint8, device=x.device)
+    sf_mma = _mma_scale_buffer(rows, K // 32, x.device)
     _lib.call("brc_cast_mxfp8", x.data_ptr(), _IN_DT[x.dtype], rows, K, _FMT[fmt],
               codes.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
     _remember(codes, (scale, None), sf_mma=sf_mma)
@@ -297,7 +308,7 @@ def _cast_nvfp4(x, recipe, ST, L, st):
     codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
     packed = torch.empty(x.shape[:-1] + (K // 2,), dtype=torch.uint8, device=x.device)
     scale = torch.empty(x.shape[:-1] + (K // 16,), dtype=torch.uint8, device=x.device)
-    sf_mma = torch.zeros(_mma_scale_shape(rows, K // 16), dtype=torch.uint8, device=x.device)
+    sf_mma = _mma_scale_buffer(rows, K // 16, x.device)
     _lib.call("brc_cast_nvfp4", x.data_ptr(), _IN_DT[x.dtype], rows, K, codes.data_ptr(),
               packed.data_ptr(), scale.data_ptr(), sf_mma.data_ptr(), st)
     _remember(codes, (scale, None), packed=packed, sf_mma=sf_mma)
@@ -407,7 +418,7 @@ def requantize(scaled, recipe):
         dev = codes.device
         out = torch.empty(codes.shape, dtype=torch.uint8, device=dev)
         scale = torch.empty(codes.shape[:-1] + (K // 32,), dtype=torch.uint8, device=dev)
-        sf_mma = torch.zeros(_mma_scale_shape(rows, K // 32), dtype=torch.uint8, device=dev)
+        sf_mma = _mma_scale_buffer(rows, K // 32, dev)
         with torch.cuda.device(dev):
             _lib.call("brc_requant_nvfp4_to_mxfp8", codes.data_ptr(),
                       _aligned(scaled.scale).data_ptr(), rows, K, _FMT[recipe.fp8_format],
