@@ -707,7 +707,7 @@ def run_ours(args):
 
     extras, libref = {}, None
     if world == 1 and not args.no_per_recipe:
-        extras = per_recipe(peaks, src)
+        extras = per_recipe(peaks, src, uuid)
         torch.cuda.empty_cache()
         libref = library_reference(peaks)
         if libref and libref.get("c2_pertensor_fp8", {}).get("TFLOP/s"):
@@ -858,7 +858,7 @@ def sharded_configs(peaks, args):
 # --------------------------------------------------------------- per recipe
 
 
-def per_recipe(peaks, src):
+def per_recipe(peaks, src, uuid=None):
     """Every BASELINE config at full size on one GPU. Casts, dequantize and
     requantize in GB/s of algorithmic bytes (input read once -- twice for
     per-tensor, whose global amax must be known before any code is written
@@ -879,11 +879,30 @@ def per_recipe(peaks, src):
     def copies(x, nbytes):
         return [x] + [x.clone() for _ in range(_rotation(nbytes) - 1)]
 
+    clk_of = {}
+
+    def timed(fns, reps=None, name=None):
+        """_time_graph after a 0.2 s idle, with enough replays for a >= 20 ms
+        window, while NVML samples the SM clock (recorded per entry: entries
+        that follow GEMM loops can run at reduced clocks)."""
+        time.sleep(0.2)
+        n = len(fns) if isinstance(fns, (list, tuple)) else 1
+        if reps is None:
+            est = _time_graph(fns)
+            reps = max(2, math.ceil(20.0 / max(est * n, 1e-3)))
+        with Clocks(uuid) as clk:
+            ms = _time_graph(fns, reps=reps)
+        c = clk.summary()
+        if name is not None:
+            clk_of[name] = {"sm_mhz": c["sm_mhz"], "reasons": c["reasons"]}
+        return ms
+
     def bw_entry(name, fns, bytes_, **extra):
-        ms = _time_graph(fns)
+        ms = timed(fns, name=name)
         gbs = bytes_ / (ms * 1e-3) / 1e9
         res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
-                     "rotated_copies": len(fns) if isinstance(fns, list) else 1, **extra}
+                     "rotated_copies": len(fns) if isinstance(fns, list) else 1, **extra,
+                     **clk_of.get(name, {})}
 
     def cast_entry(name, x, r, bytes_, **kw):
         xs = copies(x, bytes_)
@@ -898,16 +917,17 @@ def per_recipe(peaks, src):
     def ste_entry(name, x, r, bytes_):
         # fused cast_ste forward vs the unfused cast -> dequantize -> x + (y - x)
         xs = copies(x, bytes_)
-        ms_u = _time_graph([lambda xi=xi: xi + (bb.dequantize(bb.cast(xi, r)) - xi) for xi in xs])
+        ms_u = timed([lambda xi=xi: xi + (bb.dequantize(bb.cast(xi, r)) - xi) for xi in xs])
         bw_entry(name, [lambda xi=xi: bb.cast_ste(xi, r) for xi in xs], bytes_, unfused_ms=ms_u)
         del xs
 
     def gemm_entry(name, make_pair, m, n, k, peak, op_bytes, out_dtype=torch.bfloat16):
         pairs = [make_pair() for _ in range(_rotation(op_bytes))]
-        ms = _time_graph([lambda p=p: bb.linear(p[0], p[1], out_dtype=out_dtype) for p in pairs])
+        ms = timed([lambda p=p: bb.linear(p[0], p[1], out_dtype=out_dtype) for p in pairs],
+                   name=name)
         tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
         res[name] = {"ms": ms, "TFLOP/s": tf, "frac_peak": tf / peak,
-                     "rotated_copies": len(pairs)}
+                     "rotated_copies": len(pairs), **clk_of.get(name, {})}
         del pairs
 
     # C1 Float8BlockScaling: A f32 (2048, 7168) 1x128; W^T f32 (4096, 7168) 128x128
@@ -922,12 +942,13 @@ def per_recipe(peaks, src):
     gemm_entry("c1_gemm_block_fp8_f32out", lambda: (bb.cast(A, r), bb.cast(Wt, r, block_m=128)),
                2048, 4096, 7168, fp8, (A.numel() + Wt.numel()), out_dtype=torch.float32)
     As, Ws = copies(A, A.numel() * 5), copies(Wt, Wt.numel() * 5)
-    ms = _time_graph([lambda a=a, w=w: bb.linear(bb.cast(a, r), bb.cast(w, r, block_m=128),
-                                                 out_dtype=torch.float32)
-                      for a, w in zip(As, Ws)])
-    res["c1_step_cast_both_gemm_block_fp8_f32out"] = {
+    name = "c1_step_cast_both_gemm_block_fp8_f32out"
+    ms = timed([lambda a=a, w=w: bb.linear(bb.cast(a, r), bb.cast(w, r, block_m=128),
+                                           out_dtype=torch.float32)
+                for a, w in zip(As, Ws)], name=name)
+    res[name] = {
         "ms": ms, "TFLOP/s": 2.0 * 2048 * 4096 * 7168 / (ms * 1e-3) / 1e12,
-        "rotated_copies": len(As)}
+        "rotated_copies": len(As), **clk_of.get(name, {})}
     del A, Wt, sa, As, Ws
 
     # C2 per-tensor: A bf16 (16384, 8192) -- two reads + one write; W^T bf16 (8192, 8192)
@@ -944,10 +965,11 @@ def per_recipe(peaks, src):
     hist = bb.AmaxHistory(rd.amax_history_len)
     bb.cast(A, rd, amax_history=hist)  # first call: the reference cast, records the amax
     cast_entry("c2_cast_A_delayed_history_bf16", A, rd, A.numel() * 3, amax_history=hist)
-    ms = _time_graph(lambda: bb.linear(bb.cast(A, rd, amax_history=hist), bb.cast(Wt, rc),
-                                       out_dtype=torch.bfloat16), reps=10)
-    res["c2_step_delayed_A_current_W_gemm"] = {
-        "ms": ms, "TFLOP/s": FLOPS / (ms * 1e-3) / 1e12,
+    name = "c2_step_delayed_A_current_W_gemm"
+    ms = timed(lambda: bb.linear(bb.cast(A, rd, amax_history=hist), bb.cast(Wt, rc),
+                                 out_dtype=torch.bfloat16), reps=10, name=name)
+    res[name] = {
+        "ms": ms, "TFLOP/s": FLOPS / (ms * 1e-3) / 1e12, **clk_of.get(name, {}),
         "what": "C2 step with the activation cast from its amax history (one pass) instead of "
                 "the current amax (two passes); same GEMM"}
     # The activation cast fused into the GEMM (cast_matmul: two warps per CTA
@@ -966,11 +988,14 @@ def per_recipe(peaks, src):
                                                 fused=True),
     }
     times = {k: [] for k in variants}
-    for _ in range(3):
-        for k, f in variants.items():
-            times[k].append(_time_graph(f, reps=8))
+    time.sleep(0.2)
+    with Clocks(uuid) as clk:
+        for _ in range(3):
+            for k, f in variants.items():
+                times[k].append(_time_graph(f, reps=8))
     entry = {"what": "C2 activation cast + GEMM (weight cast beforehand): the cast fused into the "
-                     "GEMM launch vs a separate cast kernel; same codes and product bit for bit"}
+                     "GEMM launch vs a separate cast kernel; same codes and product bit for bit",
+             "sm_mhz": clk.summary()["sm_mhz"], "reasons": clk.summary()["reasons"]}
     for k, v in times.items():
         ms = statistics.median(v)
         entry[k] = {"ms": ms, "TFLOP/s": FLOPS / (ms * 1e-3) / 1e12}
@@ -1049,13 +1074,14 @@ def per_recipe(peaks, src):
     del Wt
     for m in (1, 4, 16):
         A = torch.randn(m, 8192, generator=g, device=dev).to(torch.bfloat16)
-        ms = _time_graph([lambda sw=sw: bb.linear(A, sw, out_dtype=torch.bfloat16)
-                          for sw in sws], reps=8)
+        name = f"c5_gemv_int4_M{m}"
+        ms = timed([lambda sw=sw: bb.linear(A, sw, out_dtype=torch.bfloat16) for sw in sws],
+                   name=name)
         b = gemv_b + m * 8192 * 2 + m * 28672 * 2
         gbs = b / (ms * 1e-3) / 1e9
-        res[f"c5_gemv_int4_M{m}"] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
-                                     "TFLOP/s": 2.0 * m * 28672 * 8192 / (ms * 1e-3) / 1e12,
-                                     "rotated_copies": len(sws)}
+        res[name] = {"ms": ms, "GB/s": gbs, "frac_hbm": gbs / hbm,
+                     "TFLOP/s": 2.0 * m * 28672 * 8192 / (ms * 1e-3) / 1e12,
+                     "rotated_copies": len(sws), **clk_of.get(name, {})}
     del sws
     torch.cuda.empty_cache()
     res["peaks"] = {"hbm_gbs": hbm, "fp8_tflops": fp8, "fp4_tflops": fp4,
