@@ -68,34 +68,51 @@ __global__ void __launch_bounds__(kThreads) k_pack(const uint8_t* __restrict__ c
   }
 }
 
-// 16 packed bytes (high-first) -> 32 codes and/or 16 bytes in the tensor-core
-// order per thread step (packed and packed_lo 16-byte aligned on this path).
+// 8 packed bytes (high-first) -> 16 codes and/or 8 bytes in the tensor-core
+// order per thread step, so that a warp's loads (256 bytes), code stores
+// (512 bytes) and packed stores (256 bytes) are each one contiguous run; four
+// steps' loads are in flight per thread (packed and packed_lo 16-byte
+// aligned on this path).
+__device__ __forceinline__ void unpack8_hi(const uint2 p, uint4& c, uint2& l) {
+  const uint32_t pw[2] = {p.x, p.y};
+  uint32_t cw[4], lw[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t hi = (pw[h] >> 4) & 0x0F0F0F0Fu;  // elements 0, 2, 4, 6
+    const uint32_t lo = pw[h] & 0x0F0F0F0Fu;         // elements 1, 3, 5, 7
+    cw[2 * h] = prmt(hi, lo, 0x5140u);               // 0, 1, 2, 3
+    cw[2 * h + 1] = prmt(hi, lo, 0x7362u);           // 4, 5, 6, 7
+    lw[h] = hi | (lo << 4);
+  }
+  c = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+  l = make_uint2(lw[0], lw[1]);
+}
+
 __global__ void __launch_bounds__(kThreads) k_unpack_hi(const uint8_t* __restrict__ packed,
                                                         int64_t n, uint8_t* __restrict__ codes,
                                                         uint8_t* __restrict__ packed_lo) {
-  const int64_t nv = n / 32;
-  for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < nv;
-       i += (int64_t)gridDim.x * kThreads) {
-    const uint4 p = *reinterpret_cast<const uint4*>(packed + 16 * i);
-    const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
-    uint32_t cw[8], lw[4];
+  constexpr int U = 4;
+  const int64_t nv = n / 16;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  auto emit = [&](int64_t i, const uint2 p) {
+    uint4 c;
+    uint2 l;
+    unpack8_hi(p, c, l);
+    if (codes) *reinterpret_cast<uint4*>(codes + 16 * i) = c;
+    if (packed_lo) *reinterpret_cast<uint2*>(packed_lo + 8 * i) = l;
+  };
+  int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x;
+  for (; i + (U - 1) * stride < nv; i += U * stride) {
+    uint2 p[U];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const uint32_t hi = (pw[h] >> 4) & 0x0F0F0F0Fu;  // elements 0, 2, 4, 6
-      const uint32_t lo = pw[h] & 0x0F0F0F0Fu;         // elements 1, 3, 5, 7
-      cw[2 * h] = prmt(hi, lo, 0x5140u);               // 0, 1, 2, 3
-      cw[2 * h + 1] = prmt(hi, lo, 0x7362u);           // 4, 5, 6, 7
-      lw[h] = hi | (lo << 4);
-    }
-    if (codes) {
-      *reinterpret_cast<uint4*>(codes + 32 * i) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-      *reinterpret_cast<uint4*>(codes + 32 * i + 16) = make_uint4(cw[4], cw[5], cw[6], cw[7]);
-    }
-    if (packed_lo) *reinterpret_cast<uint4*>(packed_lo + 16 * i) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    for (int u = 0; u < U; ++u) p[u] = *reinterpret_cast<const uint2*>(packed + 8 * (i + u * stride));
+#pragma unroll
+    for (int u = 0; u < U; ++u) emit(i + u * stride, p[u]);
   }
-  const int64_t done = nv * 32;
+  for (; i < nv; i += stride) emit(i, *reinterpret_cast<const uint2*>(packed + 8 * i));
+  const int64_t done = nv * 16;
   for (int64_t j = done / 2 + blockIdx.x * (int64_t)kThreads + threadIdx.x; j < n / 2;
-       j += (int64_t)gridDim.x * kThreads) {
+       j += stride) {
     const uint32_t b = packed[j];
     if (codes) {
       codes[2 * j] = (uint8_t)(b >> 4);
@@ -112,21 +129,28 @@ __global__ void __launch_bounds__(kThreads) k_scale_atoms(const uint8_t* __restr
                                                           int64_t rows, int64_t cols,
                                                           int64_t col_tiles,
                                                           uint8_t* __restrict__ atoms,
-                                                          int64_t total_words) {
+                                                          int64_t total_words, bool whole) {
+  // whole: a word's 4 scales are one aligned 32-bit load (cols % 4 == 0 and
+  // a 4-byte aligned base)
   for (int64_t wi = blockIdx.x * (int64_t)kThreads + threadIdx.x; wi < total_words;
        wi += (int64_t)gridDim.x * kThreads) {
-    // one 32-bit word = 4 consecutive columns of one row
+    // one 32-bit word = 4 consecutive columns of one row; atom indices fit
+    // 32 bits (the host checks), so the division is a 32-bit one
     const int64_t byte0 = 4 * wi;
-    const int64_t atom = byte0 >> 9;
+    const uint32_t atom = (uint32_t)(byte0 >> 9);
     const uint32_t in_atom = (uint32_t)(byte0 & 511);
-    const int64_t R = atom / col_tiles, C = atom - R * col_tiles;
-    const int64_t row = 128 * R + 32 * ((in_atom & 15u) >> 2) + (in_atom >> 4);
+    const uint32_t R = atom / (uint32_t)col_tiles, C = atom - R * (uint32_t)col_tiles;
+    const int64_t row = 128 * (int64_t)R + 32 * ((in_atom & 15u) >> 2) + (in_atom >> 4);
     uint32_t w = 0;
     if (row < rows) {
-      const uint8_t* src = scales + row * cols + 4 * C;
+      const uint8_t* src = scales + row * cols + 4 * (int64_t)C;
+      if (whole) {
+        w = *reinterpret_cast<const uint32_t*>(src);
+      } else {
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (4 * C + k < cols) w |= (uint32_t)src[k] << (8 * k);
+        for (int k = 0; k < 4; ++k)
+          if (4 * (int64_t)C + k < cols) w |= (uint32_t)src[k] << (8 * k);
+      }
     }
     *reinterpret_cast<uint32_t*>(atoms + byte0) = w;
   }
@@ -143,11 +167,13 @@ __global__ void __launch_bounds__(kThreads) k_int4_tiles(
     const void* __restrict__ zp, uint8_t* __restrict__ tiles, float* __restrict__ scale_tiles,
     float* __restrict__ zp_tiles) {
   const int64_t groups = cols / 128;
-  const int64_t pairs = rows * groups * 8;  // pairs of 8-element runs
+  const int64_t pairs = rows * groups * 8;  // pairs of 8-element runs (< 2^32: the host checks)
+  const uint32_t per_row = (uint32_t)(groups * 8);
   for (int64_t t = blockIdx.x * (int64_t)kThreads + threadIdx.x; t < pairs;
        t += (int64_t)gridDim.x * kThreads) {
-    const int64_t row = t / (groups * 8);
-    const int64_t rem = t - row * groups * 8;
+    const uint32_t t32 = (uint32_t)t;
+    const int64_t row = t32 / per_row;
+    const uint32_t rem = t32 - (uint32_t)row * per_row;
     const int64_t g = rem >> 3;
     const int j = 2 * (int)(rem & 7);  // first run of the pair
     const uint4 c = *reinterpret_cast<const uint4*>(codes + row * cols + 128 * g + 8 * j);
@@ -206,7 +232,7 @@ int brc_unpack_nibbles_hi(const uint8_t* packed, int64_t n, uint8_t* codes, uint
   if (!packed || (!codes && !packed_lo)) return BRC_ERR_NULL;
   if (!al16(packed) || (codes && !al16(codes)) || (packed_lo && !al16(packed_lo)))
     return BRC_ERR_ALIGN;
-  k_unpack_hi<<<grid_for(n / 32 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
+  k_unpack_hi<<<grid_for(n / 64 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
                                                                             packed_lo);
   return check_launch();
 }
@@ -219,8 +245,10 @@ int brc_scale_atoms(const uint8_t* scales, int64_t rows, int64_t scale_cols, uin
   if (reinterpret_cast<uintptr_t>(atoms) & 3u) return BRC_ERR_ALIGN;
   const int64_t col_tiles = (scale_cols + 3) / 4;
   const int64_t total_words = ((rows + 127) / 128) * col_tiles * 128;
+  if (total_words / 128 > 0xFFFFFFFFll) return BRC_ERR_RANGE;
+  const bool whole = scale_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0;
   k_scale_atoms<<<grid_for(total_words), kThreads, 0, (cudaStream_t)stream>>>(
-      scales, rows, scale_cols, col_tiles, atoms, total_words);
+      scales, rows, scale_cols, col_tiles, atoms, total_words, whole);
   return check_launch();
 }
 
@@ -235,6 +263,7 @@ int brc_int4_tiles(const uint8_t* codes, int64_t rows, int64_t cols, const void*
   if (scale_dtype != BRC_SCALE_F16 && scale_dtype != BRC_SCALE_F32) return BRC_ERR_DTYPE;
   if (!al16(codes) || !al16(tiles)) return BRC_ERR_ALIGN;
   const int64_t pairs = rows * (cols / 128) * 8;
+  if (pairs > 0xFFFFFFFFll) return BRC_ERR_RANGE;
   cudaStream_t st = (cudaStream_t)stream;
   if (scale_dtype == BRC_SCALE_F16)
     k_int4_tiles<true><<<grid_for(pairs), kThreads, 0, st>>>(codes, rows, cols, scales,

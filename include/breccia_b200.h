@@ -202,14 +202,15 @@ int brc_pack_codes_lo(const uint8_t* codes, int64_t n, uint8_t* packed_lo, void*
  * brc_cast_nvfp4 write) from stored one-byte scales (rows, scale_cols): MXFP8
  * E8M0 or NVFP4 E4M3 codes (cast.py:420-446, 468-496). atoms holds
  * ceil(rows/128) * ceil(scale_cols/4) * 512 bytes, every one written (padding
- * zero), 4-byte aligned. */
+ * zero), 4-byte aligned. BRC_ERR_RANGE past 2^32 atoms. */
 int brc_scale_atoms(const uint8_t* scales, int64_t rows, int64_t scale_cols, uint8_t* atoms,
                     void* stream);
 /* The INT4 skinny-GEMM tiles brc_cast_int4 writes (packed_tiles, scale_tiles,
  * zp_tiles; layout in brc_cast_int4's comment) from a stored INT4 tensor of
  * group 128: codes (rows, cols) one per byte, scales and zero_points (rows,
  * cols/128) in scale_dtype (zero_points and zp_tiles both NULL when
- * symmetric) (cast.py:516-571). rows % 16 == 0, cols % 128 == 0. */
+ * symmetric) (cast.py:516-571). rows % 16 == 0, cols % 128 == 0;
+ * BRC_ERR_RANGE when rows * cols / 16 exceeds 2^32. */
 int brc_int4_tiles(const uint8_t* codes, int64_t rows, int64_t cols, const void* scales,
                    const void* zero_points, int scale_dtype, uint8_t* tiles, float* scale_tiles,
                    float* zp_tiles, void* stream);
