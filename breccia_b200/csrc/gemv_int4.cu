@@ -457,6 +457,9 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
           const int rb = warp + o * NC;
           if (rb < nrb && rb / rbs == k) {
             const int base = (rb - k * rbs) * gpc;  // first tile of the row block in the stage
+            // two tiles per iteration: their MMA chains are independent and
+            // interleave (C5 M = 16: 61.5 -> 60.3 us)
+#pragma unroll 2
             for (int j = 0; j < gpc; ++j) {
               const int pos = base + j;
               const uint4 w0 = *reinterpret_cast<const uint4*>(sp + pos * TILE_BYTES + gid * 64 +
