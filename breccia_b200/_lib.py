@@ -54,7 +54,7 @@ PROTOTYPES = {
     "brc_gemm_fp8_pertensor": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_cast_gemm_workspace_bytes": ([_i, _i], _i64),
     "brc_cast_gemm_pertensor_fp8": ([_p, _i, _i, _p, _i, _p, _i, _i, _i, _p, _i, _i, _i, _p, _p,
-                                     _p, _i, _p, _i64, _i, _p], _i),
+                                     _p, _p, _i, _p, _i64, _i, _p], _i),
     "brc_gemm_mxfp8": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_nvfp4": ([_p, _p, _i, _i, _i, _p, _p, _p, _i, _p], _i),
     "brc_gemm_block_fp8": ([_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p], _i),

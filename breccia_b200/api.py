@@ -502,14 +502,24 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
     if not ok or fused is False:
         a = cast(x, recipe, amax_history=amax_history)
         return matmul(a, b, out_dtype, b_kmajor=b_kmajor), a
+    with torch.cuda.device(x.device):
+        w_codes = _codes_u8(b.data) if b_kmajor else gemm._transposed_codes(b)
+    return _fused_cast_gemm(x, recipe, w_codes, b, N, odt, amax_history, None, prologue_rows)
+
+
+def _fused_cast_gemm(x, recipe, w_codes, b, N, odt, amax_history, amax_word, prologue_rows):
+    """brc_cast_gemm_pertensor_fp8 on ``x`` and the (N, K) codes of the
+    per-tensor ScaledTensor ``b``; ``amax_word`` (a device int32 word holding
+    the float bits of an amax already reduced by the caller) replaces the
+    amax pass. Returns (out, cast(x))."""
     ST, L = _classes(recipe)
     fmt = recipe.fp8_format
     dev = x.device
+    K = x.shape[-1]
     M = x.numel() // K
     cdt = odt if odt in _OUT_DT else torch.float32
     with torch.cuda.device(dev):
         st = _stream(dev)
-        w_codes = _codes_u8(b.data) if b_kmajor else gemm._transposed_codes(b)
         codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
         scale = torch.empty((), dtype=torch.float32, device=dev)
         out = torch.empty(x.shape[:-1] + (N,), dtype=cdt, device=dev)
@@ -527,6 +537,7 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
         _lib.call("brc_cast_gemm_pertensor_fp8", x.data_ptr(), _IN_DT[x.dtype], _FMT[fmt],
                   w_codes.data_ptr(), _FMT[b.recipe.fp8_format],
                   b.scale.to(torch.float32).data_ptr(), M, N, K, hist, hlen, margin, use,
+                  None if amax_word is None else amax_word.data_ptr(),
                   codes.data_ptr(), scale.data_ptr(), out.data_ptr(), _OUT_DT[cdt],
                   ws.data_ptr(), ws_bytes, int(prologue_rows), st)
     if amax_history is not None:

@@ -31,7 +31,8 @@ from . import _lib
 from .api import _input, _classes, _stream, _IN_DT, _FMT, _TORCH_FP8
 
 __all__ = ["shard_rows", "allreduce_amax_word", "cast_per_tensor_sharded", "cast_sharded",
-           "cast_per_tensor_async", "PendingCast", "cast_weight_split"]
+           "cast_per_tensor_async", "PendingCast", "cast_weight_split",
+           "cast_matmul_weight_split"]
 
 
 def shard_rows(n: int, world: int, rank: int, align: int = 128):
@@ -175,3 +176,62 @@ def cast_weight_split(a, w_shard, recipe, group=None, **kw):
             out.append(ST(data=codes.view(_TORCH_FP8[fmt]), scale=scale, recipe=recipe,
                           layout=L.PerTensor()))
     return out[0], out[1]
+
+
+def cast_matmul_weight_split(a, w_shard, recipe, group=None, out_dtype=torch.bfloat16,
+                             fused=None):
+    """One layer's step in the weight-split layout with the activation's cast
+    fused into the GEMM (``cast_matmul``): the two amax words of
+    ``cast_weight_split`` (a ``1/world`` share of the activation's rows and
+    this rank's weight shard, one all-reduce(MAX) of 8 bytes), the weight
+    shard's cast, then one launch that encodes the whole activation with the
+    global amax while the tensor cores compute ``a @ w_shard^T``. Returns
+    ``(out, cast(a), cast(w_shard))``, bit-identical to ``cast_weight_split``
+    followed by ``linear``.
+
+    Every rank encodes the whole (replicated) activation while its GEMM
+    covers only ``1/world`` of the output columns. ``fused=None`` takes the
+    fused launch only where it measured no slower on B200 (a rank's N >=
+    8192, i.e. one rank); for narrower shards the in-kernel encode is the
+    slower way (N = 1024: 0.229 vs 0.169 ms for the apply pass + GEMM), so the
+    apply pass runs first. Per-tensor recipes only (others:
+    ``cast_weight_split`` + ``linear``)."""
+    from .api import _fused_cast_gemm, _torch_out_dtype, linear, _FUSED_MIN_N
+    if getattr(recipe, "name", None) not in ("delayed", "current"):
+        sa, sw = cast_weight_split(a, w_shard, recipe, group)
+        return linear(sa, sw, out_dtype), sa, sw
+    x, w = _input(a), _input(w_shard)
+    world, rank = _world(group)
+    K = x.shape[-1] if x.ndim else 1
+    rows = x.numel() // K if K else 0
+    N = w.shape[0]
+    if fused is None:
+        fused = N >= _FUSED_MIN_N
+    if not (fused and K > 0 and K % 128 == 0 and N % 16 == 0 and w.ndim == 2 and x.ndim >= 1):
+        sa, sw = cast_weight_split(a, w_shard, recipe, group)
+        return linear(sa, sw, out_dtype), sa, sw
+    lo, hi = shard_rows(rows, world, rank)
+    dev = x.device
+    words = torch.empty(2, dtype=torch.int32, device=dev)
+    fmt = recipe.fp8_format
+    ST, L = _classes(recipe)
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        _lib.call("brc_amax_reset", words.data_ptr(), st)
+        _lib.call("brc_amax_reset", words.data_ptr() + 4, st)
+        _lib.call("brc_amax_accumulate", x.data_ptr() + lo * K * x.element_size(),
+                  _IN_DT[x.dtype], (hi - lo) * K, words.data_ptr(), st)
+        _lib.call("brc_amax_accumulate", w.data_ptr(), _IN_DT[w.dtype], w.numel(),
+                  words.data_ptr() + 4, st)
+    if world > 1:
+        dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group)
+    with torch.cuda.device(dev):
+        st = _stream(dev)
+        wc = torch.empty(w.shape, dtype=torch.uint8, device=dev)
+        wsc = torch.empty((), dtype=torch.float32, device=dev)
+        _lib.call("brc_cast_pertensor_fp8_apply", w.data_ptr(), _IN_DT[w.dtype], w.numel(),
+                  _FMT[fmt], words.data_ptr() + 4, wc.data_ptr(), wsc.data_ptr(), st)
+    sw = ST(data=wc.view(_TORCH_FP8[fmt]), scale=wsc, recipe=recipe, layout=L.PerTensor())
+    out, sa = _fused_cast_gemm(x, recipe, wc, sw, N, _torch_out_dtype(out_dtype), None,
+                               words[0:1], -1)
+    return out, sa, sw

@@ -293,15 +293,19 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
  * use_history == 0) or brc_cast_pertensor_fp8_delayed (history, use_history)
  * followed by brc_gemm_fp8_pertensor, bit for bit: a_codes / a_scale_out are
  * the cast's, d the GEMM's; with a history its ring receives x's amax.
+ * amax_in (no history): the float32 bit pattern of the amax to scale with,
+ * already reduced by the caller (the whole tensor's amax when x is one of
+ * several ranks' copies or shards): brc_cast_pertensor_fp8_apply with that
+ * word, then the GEMM; no amax pass here.
  * workspace: device scratch of brc_cast_gemm_workspace_bytes(M, K) bytes
  * (zeroed here). K % 128 == 0, N % 16 == 0, 16-byte aligned pointers. */
 int64_t brc_cast_gemm_workspace_bytes(int M, int K);
 int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uint8_t* b,
                                 int b_fmt, const float* b_scale, int M, int N, int K,
                                 float* history, int history_len, int margin, int use_history,
-                                uint8_t* a_codes, float* a_scale_out, void* d, int d_dtype,
-                                void* workspace, int64_t workspace_bytes, int prologue_rows,
-                                void* stream);
+                                const uint32_t* amax_in, uint8_t* a_codes, float* a_scale_out,
+                                void* d, int d_dtype, void* workspace, int64_t workspace_bytes,
+                                int prologue_rows, void* stream);
 /* MXFP8: scales in the tcgen05 layout written by brc_cast_mxfp8 (scales_mma)
  * for A (M rows) and B (N rows). K % 128 == 0. */
 int brc_gemm_mxfp8(const uint8_t* a, const uint8_t* b, int M, int N, int K, int a_fmt,

@@ -217,3 +217,62 @@ def test_fused_arguments():
     with pytest.raises(ValueError):
         bb.cast_matmul(torch.randn(256, 512, device="cuda"), w, bb.Float8CurrentScaling(),
                        b_kmajor=True)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 1024, 4096), (2048, 256, 2048), (8192, 512, 1024)])
+def test_fused_narrow_n(M, N, K):
+    """Weight-split shapes (a rank's few output columns): the GEMM is short, so
+    most of A is encoded while few tiles are left to overlap with."""
+    import breccia_b200 as bb
+    g = torch.Generator().manual_seed(M + N)
+    x = (torch.randn(M, K, generator=g) * 2).to(torch.bfloat16).cuda()
+    w = _weight(N, K)
+    _check_against_unfused(x, w, bb.Float8CurrentScaling(), out_dtype=torch.bfloat16,
+                           fused=True, prologue_rows=0)
+
+
+def test_fused_with_reduced_amax():
+    """An amax reduced elsewhere (another rank's larger values): the codes equal
+    the apply pass with that amax word, the product the GEMM on those codes."""
+    import breccia_b200 as bb
+    from breccia_b200 import _lib
+    from breccia_b200.api import _fused_cast_gemm
+    g = torch.Generator().manual_seed(21)
+    M, N, K = 1536, 1024, 2048
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    w = _weight(N, K)
+    r = bb.Float8CurrentScaling()
+    st = torch.cuda.current_stream().cuda_stream
+    for amax in (float(x.float().abs().max()), 37.5):
+        word = torch.tensor([np.float32(amax).view(np.int32)], dtype=torch.int32, device="cuda")
+        out, a = _fused_cast_gemm(x, r, w.data.view(torch.uint8), w, N, torch.bfloat16, None,
+                                  word, 0)
+        codes = torch.empty(M, K, dtype=torch.uint8, device="cuda")
+        scale = torch.empty((), dtype=torch.float32, device="cuda")
+        _lib.call("brc_cast_pertensor_fp8_apply", x.data_ptr(), _lib.DTYPE_BF16, x.numel(),
+                  _lib.FP8_E4M3, word.data_ptr(), codes.data_ptr(), scale.data_ptr(), st)
+        torch.cuda.synchronize()
+        assert torch.equal(a.data.view(torch.uint8), codes)
+        assert same_bits(np.atleast_1d(a.scale.cpu().numpy()), np.atleast_1d(scale.cpu().numpy()))
+        ref = bb.linear(bb.ScaledTensor(data=codes.view(torch.float8_e4m3fn), scale=scale,
+                                        recipe=r, layout=bb.PerTensor()),
+                        w, out_dtype=torch.bfloat16)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_fused_weight_split_single_rank():
+    """cast_matmul_weight_split without a process group equals
+    cast_weight_split followed by linear, bit for bit."""
+    import breccia_b200 as bb
+    from breccia_b200.dist import cast_matmul_weight_split, cast_weight_split
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(2048, 2048, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(768, 2048, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    r = bb.Float8CurrentScaling()
+    out, sa, sw = cast_matmul_weight_split(x, w, r, fused=True)
+    sa2, sw2 = cast_weight_split(x, w, r)
+    out2 = bb.linear(sa2, sw2, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(sa.data.view(torch.uint8), sa2.data.view(torch.uint8))
+    assert torch.equal(sw.data.view(torch.uint8), sw2.data.view(torch.uint8))
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))

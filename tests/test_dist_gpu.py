@@ -5,7 +5,9 @@ through ``dist.cast_weight_split`` (per-tensor recipes: one all-reduce(MAX)
 of two amax words) and computes its C[:, n0:n1]. Codes and scales must equal
 the single-GPU casts bit for bit; the concatenated C must equal the
 single-GPU GEMM up to float32 summation order (the shard may take a
-different GEMM kernel shape). Skipped where fewer than 2 GPUs are visible.
+different GEMM kernel shape). ``cast_matmul_weight_split`` (the activation's
+cast fused into the GEMM) must equal ``cast_weight_split`` + ``linear`` on
+each rank bit for bit. Skipped where fewer than 2 GPUs are visible.
 """
 
 import os
@@ -47,16 +49,22 @@ def _rank_main(rank, world, port, q):
                             timeout=timedelta(seconds=60))
     try:
         import breccia_b200 as bb
-        from breccia_b200.dist import shard_rows, cast_weight_split
+        from breccia_b200.dist import shard_rows, cast_weight_split, cast_matmul_weight_split
         A, Wt = _inputs()
         n0, n1 = shard_rows(Wt.shape[0], world, rank)
         for name in RECIPES:
             sa, sw = cast_weight_split(A.to(dev), Wt[n0:n1].to(dev), _recipe(name))
             c = bb.linear(sa, sw, out_dtype=torch.float32)
+            # the same step with the activation's cast fused into the GEMM
+            cf, saf, swf = cast_matmul_weight_split(A.to(dev), Wt[n0:n1].to(dev), _recipe(name),
+                                                    out_dtype=torch.float32, fused=True)
             torch.cuda.synchronize()
+            fused_same = bool(torch.equal(cf.view(torch.int32), c.view(torch.int32)) and
+                              torch.equal(saf.data.view(torch.uint8), sa.data.view(torch.uint8)) and
+                              torch.equal(swf.data.view(torch.uint8), sw.data.view(torch.uint8)))
             q.put((name, rank, n0, n1, c.cpu().numpy(),
                    sw.data.view(torch.uint8).cpu().numpy(), sw.scale.cpu().numpy(),
-                   sa.scale.cpu().numpy()))
+                   sa.scale.cpu().numpy(), fused_same))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -91,7 +99,8 @@ def test_weight_split_two_gpus_equals_one_gpu():
         parts = sorted((t for t in got if t[0] == name), key=lambda t: t[1])
         c = np.concatenate([t[4] for t in parts], axis=1)
         assert np.abs(c - full).max() <= 1e-6 * np.abs(full).max(), name
-        for _, _, n0, n1, _, sh_codes, sh_scale, a_scale in parts:
+        for _, _, n0, n1, _, sh_codes, sh_scale, a_scale, fused_same in parts:
+            assert fused_same, name
             assert np.array_equal(sh_codes, codes[n0:n1]), name
             want = scale if name == "current" else scale[n0:n1]
             assert np.array_equal(np.atleast_1d(sh_scale).view(np.uint8),
