@@ -1211,6 +1211,8 @@ NCU_CASES = {
     "cast_block2d": "128x128 block FP8 cast, f32 4096x7168",
     "requant_nv_mx": "NVFP4 -> MXFP8 requantize, 8192x8192",
     "dequant_mxfp8": "MXFP8 dequantize to f32, 8192x8192",
+    "unpack_nvfp4": "packed 4-bit load (breccia's nibble order) -> codes + tensor-core packed "
+                    "order, 16384x16384",
 }
 
 
@@ -1246,6 +1248,14 @@ def run_ncu_case(name):
     elif name == "dequant_mxfp8":
         st = bb.cast(bf16(8192, 8192), bb.MXFP8BlockScaling())
         fn = lambda: bb.dequantize(st)  # noqa: E731
+    elif name == "unpack_nvfp4":
+        from breccia_b200 import _lib as L
+        n = 16384 * 16384
+        pk = torch.randint(0, 256, (n // 2,), generator=g, device=dev, dtype=torch.uint8)
+        codes = torch.empty(n, dtype=torch.uint8, device=dev)
+        lo = torch.empty(n // 2, dtype=torch.uint8, device=dev)
+        fn = lambda: L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes.data_ptr(),  # noqa: E731
+                            lo.data_ptr(), torch.cuda.current_stream().cuda_stream)
     else:
         x, r, kw = {
             "cast_pertensor": (lambda: bf16(16384, 8192), bb.Float8CurrentScaling(), {}),
