@@ -70,9 +70,10 @@ __global__ void __launch_bounds__(kThreads) k_pack(const uint8_t* __restrict__ c
 
 // 8 packed bytes (high-first) -> 16 codes and/or 8 bytes in the tensor-core
 // order per thread step, so that a warp's loads (256 bytes), code stores
-// (512 bytes) and packed stores (256 bytes) are each one contiguous run; four
-// steps' loads are in flight per thread (packed and packed_lo 16-byte
-// aligned on this path).
+// (512 bytes) and packed stores (256 bytes) are each one contiguous run; eight
+// steps' loads are in flight per thread (the kernel waits on memory: with
+// four, ncu put 46 cycles of long-scoreboard stall on every issued
+// instruction). packed and packed_lo are 16-byte aligned on this path.
 __device__ __forceinline__ void unpack8_hi(const uint2 p, uint4& c, uint2& l) {
   const uint32_t pw[2] = {p.x, p.y};
   uint32_t cw[4], lw[2];
@@ -91,7 +92,7 @@ __device__ __forceinline__ void unpack8_hi(const uint2 p, uint4& c, uint2& l) {
 __global__ void __launch_bounds__(kThreads) k_unpack_hi(const uint8_t* __restrict__ packed,
                                                         int64_t n, uint8_t* __restrict__ codes,
                                                         uint8_t* __restrict__ packed_lo) {
-  constexpr int U = 4;
+  constexpr int U = 8;
   const int64_t nv = n / 16;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   auto emit = [&](int64_t i, const uint2 p) {
@@ -232,7 +233,7 @@ int brc_unpack_nibbles_hi(const uint8_t* packed, int64_t n, uint8_t* codes, uint
   if (!packed || (!codes && !packed_lo)) return BRC_ERR_NULL;
   if (!al16(packed) || (codes && !al16(codes)) || (packed_lo && !al16(packed_lo)))
     return BRC_ERR_ALIGN;
-  k_unpack_hi<<<grid_for(n / 64 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
+  k_unpack_hi<<<grid_for(n / 128 + 1), kThreads, 0, (cudaStream_t)stream>>>(packed, n, codes,
                                                                             packed_lo);
   return check_launch();
 }
