@@ -28,7 +28,10 @@ import numpy as np
 import pytest
 import torch
 
-REFERENCE_SRC = os.environ.get("BRECCIA_REFERENCE_SRC", "/root/reference/src")
+# the reference checkout next to this repository's, unless the variable names one
+_BESIDE = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                       "reference", "src")
+REFERENCE_SRC = os.environ.get("BRECCIA_REFERENCE_SRC", _BESIDE)
 
 
 @pytest.fixture
