@@ -136,27 +136,60 @@ struct LaneVals {
 // x + (y - x) in float32, as the reference's x + (y - x).detach() evaluates it.
 // The values go straight to this lane's slot of the warp's shared-memory
 // stage (16 bytes at a time), so no register array holds them.
+// FP8 pairs to f16 pairs by the hardware conversion: every E4M3 / E5M2 value
+// (subnormals, infinities and NaN included) is exact in float16 and again in
+// float32, so the float32 product below rounds exactly once, as the
+// reference's decode-then-multiply does. Byte i of the pair lands in half i.
+template <int FMT>
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint16_t b = (uint16_t)two;
+  if constexpr (FMT == BRC_FP8_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(b));
+  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(b));
+  return d;
+}
+// Two E2M1 codes (one per byte, low nibbles) to f16 pairs, exactly.
+__device__ __forceinline__ uint32_t e2m1_bytes_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint32_t pair = (two & 0x0Fu) | ((two >> 4) & 0xF0u);
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(d)
+      : "r"(pair));
+  return d;
+}
+__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
+  const __half2 v = *reinterpret_cast<const __half2*>(&h);
+  lo = __low2float(v);
+  hi = __high2float(v);
+}
+
 template <int MODE, int FMT, int NW>
 __device__ __forceinline__ void ste_values(const BlockCastArgs& a, const float* f,
                                            const uint32_t* w, float dqs, float dqz, float* o) {
 #pragma unroll
   for (int j = 0; j < NW; ++j) {
-    float q[4];
+    float q[4], d[4];
+    if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
+      // hardware pair conversions (exact; a NaN code's sign and payload do
+      // not reach the result: the float32 arithmetic below returns the
+      // canonical NaN for any NaN operand)
+      f16x2_to_f32(fp8x2_to_f16x2<FMT>(w[j]), d[0], d[1]);
+      f16x2_to_f32(fp8x2_to_f16x2<FMT>(w[j] >> 16), d[2], d[3]);
+    } else if constexpr (MODE == kNvfp4) {
+      f16x2_to_f32(e2m1_bytes_to_f16x2(w[j]), d[0], d[1]);
+      f16x2_to_f32(e2m1_bytes_to_f16x2(w[j] >> 16), d[2], d[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = (w[j] >> (8 * i)) & 0xFu;
+        d[i] = (MODE == kInt4Sym && a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+        if constexpr (MODE == kInt4Asym) d[i] = __fsub_rn(d[i], dqz);
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t code = (w[j] >> (8 * i)) & 0xFFu;
-      float d;
-      if constexpr (MODE == kBlockFp8 || MODE == kMxfp8) {
-        d = dec_fp8<FMT>(code);
-      } else if constexpr (MODE == kNvfp4) {
-        d = dec_e2m1(code);
-      } else {
-        const uint32_t lo = code & 0xFu;
-        d = (MODE == kInt4Sym && a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
-        if constexpr (MODE == kInt4Asym) d = __fsub_rn(d, dqz);
-      }
       const float x = f[4 * j + i];
-      q[i] = __fadd_rn(x, __fsub_rn(__fmul_rn(d, dqs), x));
+      q[i] = __fadd_rn(x, __fsub_rn(__fmul_rn(d[i], dqs), x));
     }
     *reinterpret_cast<float4*>(o + 4 * j) = make_float4(q[0], q[1], q[2], q[3]);
   }
@@ -613,9 +646,14 @@ __global__ void __launch_bounds__(256) k_pertensor_apply(const void* __restrict_
       if constexpr (STE) {
 #pragma unroll
         for (int j = 0; j < V / 4; ++j) {
-          float o[4];
+          // the fast path's codes are finite: decode them by the hardware pair
+          // conversions (exact), then ste1's arithmetic
+          float o[4], d[4];
+          f16x2_to_f32(fp8x2_to_f16x2<FMT>(w0[j]), d[0], d[1]);
+          f16x2_to_f32(fp8x2_to_f16x2<FMT>(w0[j] >> 16), d[2], d[3]);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) o[q] = ste1<FMT>(f0[4 * j + q], (w0[j] >> (8 * q)) & 0xFFu, s);
+          for (int q = 0; q < 4; ++q)
+            o[q] = __fadd_rn(f0[4 * j + q], __fsub_rn(__fmul_rn(d[q], s), f0[4 * j + q]));
           stg16(ste_out + vi * V + 4 * j, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]),
                                                       __float_as_uint(o[2]), __float_as_uint(o[3])));
         }
@@ -904,33 +942,6 @@ __device__ __forceinline__ void store_out16(void* out, int64_t e0, const float* 
     stg16(o, make_uint4(w[0], w[1], w[2], w[3]));
     stg16(o + 16, make_uint4(w[4], w[5], w[6], w[7]));
   }
-}
-
-// FP8 pairs to f16 pairs by the hardware conversion: every E4M3 / E5M2 value
-// (subnormals, infinities and NaN included) is exact in float16 and again in
-// float32, so the float32 product below rounds exactly once, as the
-// reference's decode-then-multiply does. Byte i of the pair lands in half i.
-template <int FMT>
-__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
-  uint32_t d;
-  const uint16_t b = (uint16_t)two;
-  if constexpr (FMT == BRC_FP8_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(b));
-  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(b));
-  return d;
-}
-// Two E2M1 codes (one per byte, low nibbles) to f16 pairs, exactly.
-__device__ __forceinline__ uint32_t e2m1_bytes_to_f16x2(uint32_t two) {
-  uint32_t d;
-  const uint32_t pair = (two & 0x0Fu) | ((two >> 4) & 0xF0u);
-  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
-      : "=r"(d)
-      : "r"(pair));
-  return d;
-}
-__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
-  const __half2 v = *reinterpret_cast<const __half2*>(&h);
-  lo = __low2float(v);
-  hi = __high2float(v);
 }
 
 __device__ __forceinline__ uint32_t ldg4(const void* p) {
