@@ -120,3 +120,50 @@ def test_bridge_entry_points_reject_bad_arguments():
     assert L.brc_int4_tiles(p, 15, 128, p, None, 0, p, p, None, None) == _lib.BRC_ERR_UNSUPPORTED
     assert L.brc_int4_tiles(p, 16, 96, p, None, 0, p, p, None, None) == _lib.BRC_ERR_UNSUPPORTED
     assert L.brc_int4_tiles(p, 16, 128, p, None, 7, p, p, None, None) == _lib.BRC_ERR_DTYPE
+
+
+def test_fused_cast_gemm_rejects_bad_arguments():
+    """brc_cast_gemm_pertensor_fp8 / brc_cast_pertensor_fp8_delayed check
+    everything on the host before the first CUDA call."""
+    L = _lib.lib()
+    _, p = _buf(4096)
+    ws = L.brc_cast_gemm_workspace_bytes(256, 2048)
+    assert ws == 16 + 4 * 1 * 2  # one 256-row block, two 1024-wide K chunks
+    assert L.brc_cast_gemm_workspace_bytes(-1, 128) == -1
+
+    def call(**kw):
+        a = dict(x=p, x_dtype=_lib.DTYPE_BF16, a_fmt=_lib.FP8_E4M3, b=p, b_fmt=_lib.FP8_E4M3,
+                 b_scale=p, M=256, N=256, K=2048, history=None, history_len=0, margin=0,
+                 use_history=0, amax_in=None, a_codes=p, a_scale=p, d=p,
+                 d_dtype=_lib.DTYPE_BF16, ws=p, ws_bytes=ws, prologue=-1)
+        a.update(kw)
+        return L.brc_cast_gemm_pertensor_fp8(
+            a["x"], a["x_dtype"], a["a_fmt"], a["b"], a["b_fmt"], a["b_scale"], a["M"], a["N"],
+            a["K"], a["history"], a["history_len"], a["margin"], a["use_history"], a["amax_in"],
+            a["a_codes"], a["a_scale"], a["d"], a["d_dtype"], a["ws"], a["ws_bytes"],
+            a["prologue"], None)
+
+    assert call(a_codes=None) == _lib.BRC_ERR_NULL
+    assert call(ws=None) == _lib.BRC_ERR_NULL
+    assert call(b_scale=None) == _lib.BRC_ERR_NULL
+    assert call(x_dtype=7) == _lib.BRC_ERR_DTYPE
+    assert call(a_fmt=5) == _lib.BRC_ERR_DTYPE
+    assert call(d_dtype=9) == _lib.BRC_ERR_DTYPE
+    assert call(K=2000) == _lib.BRC_ERR_UNSUPPORTED     # K % 128
+    assert call(N=250) == _lib.BRC_ERR_UNSUPPORTED      # N % 16
+    assert call(x=p + 8) == _lib.BRC_ERR_ALIGN
+    assert call(a_codes=p + 4) == _lib.BRC_ERR_ALIGN
+    assert call(history=p, history_len=0) == _lib.BRC_ERR_SHAPE
+    assert call(history=p, history_len=4, amax_in=p) == _lib.BRC_ERR_UNSUPPORTED
+    assert call(margin=200) == _lib.BRC_ERR_RANGE
+    assert call(ws_bytes=ws - 4) == _lib.BRC_ERR_SHAPE
+    assert call(M=-1) == _lib.BRC_ERR_SHAPE
+    # the delayed cast's own checks
+    assert L.brc_cast_pertensor_fp8_delayed(p, 1, 64, 0, None, 4, 0, 1, p, p, p,
+                                            None) == _lib.BRC_ERR_NULL
+    assert L.brc_cast_pertensor_fp8_delayed(p, 1, 64, 0, p, 0, 0, 1, p, p, p,
+                                            None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_cast_pertensor_fp8_delayed(p, 1, 64, 0, p, 4, -127, 1, p, p, p,
+                                            None) == _lib.BRC_ERR_RANGE
+    assert L.brc_cast_pertensor_fp8_delayed(p, 9, 64, 0, p, 4, 0, 1, p, p, p,
+                                            None) == _lib.BRC_ERR_DTYPE
