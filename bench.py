@@ -66,11 +66,15 @@ METRIC = "scaled-matmul TFLOP/s (C2 per-tensor FP8: cast A + cast W + GEMM, whol
 L2_BYTES = 126e6
 
 # DRAM bytes (read + write) of one launch of the headline GEMM on one GPU,
-# from one ncu capture of `bench.py --steps 1 --warmup 3 --no-e2e
-# --no-cpu-baseline --no-per-recipe --no-sharded` (dram__bytes_read.sum
-# 679.50 MB + dram__bytes_write.sum 248.64 MB). Reported as the roofline's
-# `traffic` with its source; it is not measured inside this run.
-GEMM_DRAM_BYTES = 679.50e6 + 248.64e6
+# from one one-pass ncu capture (`--metrics gpu__time_duration.sum,
+# sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active,
+# dram__bytes_read.sum,dram__bytes_write.sum -k regex:k_gemm_pair -c 1`) of
+# `bench.py --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-per-recipe
+# --no-sharded --no-parity`: dram__bytes_read.sum 838.52 MB +
+# dram__bytes_write.sum 251.04 MB (cold L2: ncu flushes caches before the
+# launch). Reported as the roofline's `traffic` with its source; it is not
+# measured inside this run.
+GEMM_DRAM_BYTES = 838.52e6 + 251.04e6
 
 
 def parse():
