@@ -515,25 +515,29 @@ def run_ours(args):
     for _ in range(args.warmup):
         out = step(A, Wt_sh)
     _barrier()
-    # One step is captured as a CUDA graph (its 7 kernels and, with N > 1, its
-    # NCCL all-reduce) and replayed. Issued from Python the step costs the host
-    # more than the device once the GEMM is split 8 ways (8 ranks' processes
-    # share the host), so the GPUs would idle between launches. Every rank
-    # agrees on graph or eager timing before any replay.
+    # S consecutive steps (S divides K) are captured as one CUDA graph (7
+    # kernels per step and, with N > 1, its NCCL all-reduce) and replayed K / S
+    # times. Issued from Python the step costs the host more than the device
+    # once the GEMM is split 8 ways (8 ranks' processes share the host), so the
+    # GPUs would idle between launches. Each captured step has its own pair of
+    # events around the GEMM (event record nodes); after the timed loop they
+    # hold the GEMM times of the last S steps of the timed region itself. Every
+    # rank agrees on graph or eager timing before any replay.
+    S = next(d for d in (5, 4, 3, 2, 1) if args.steps % d == 0)
     graph, timing = None, "eager launches from Python"
-    # events around the GEMM inside the step (in the graph: event record nodes)
     marks = None
     if not args.eager:
         err = ""
         try:
-            marks = (torch.cuda.Event(enable_timing=True, external=True),
-                     torch.cuda.Event(enable_timing=True, external=True))
+            marks = [(torch.cuda.Event(enable_timing=True, external=True),
+                      torch.cuda.Event(enable_timing=True, external=True)) for _ in range(S)]
             graph = torch.cuda.CUDAGraph()
             cs = torch.cuda.Stream()
             cs.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(cs):
                 with torch.cuda.graph(graph, stream=cs):
-                    out = step(A, Wt_sh, marks)
+                    for mk in marks:
+                        out = step(A, Wt_sh, mk)
             torch.cuda.current_stream().wait_stream(cs)
             torch.cuda.synchronize()
         except Exception as e:  # capture refused on this rank
@@ -544,8 +548,9 @@ def run_ours(args):
             timing = "eager launches from Python (CUDA-graph capture failed: " + (err or "on another rank") + ")"
         else:
             graph.replay()
-            timing = ("one step captured as a CUDA graph (7 kernels" +
-                      (" + 1 NCCL all-reduce" if world > 1 else "") + "), replayed per step")
+            timing = (f"{S} steps captured as one CUDA graph ({7 * S} kernels" +
+                      (f" + {S} NCCL all-reduces" if world > 1 else "") +
+                      f"), replayed {args.steps // S} times")
     _barrier()
     props = torch.cuda.get_device_properties(dev)
     uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else None
@@ -553,57 +558,31 @@ def run_ours(args):
     t_end = torch.cuda.Event(enable_timing=True)
     with Clocks(uuid) as clk:
         t_start.record()
-        for _ in range(args.steps):
-            if graph is not None:
+        if graph is not None:
+            for _ in range(args.steps // S):
                 graph.replay()
-            else:
+        else:
+            for _ in range(args.steps):
                 out = step(A, Wt_sh)
         t_end.record()
         torch.cuda.synchronize()
     _barrier()
     ms = t_start.elapsed_time(t_end) / args.steps
-    # The GEMM inside the step: events around it. With graphs, four steps are
-    # captured back to back, each with its own event pair, and the GEMMs of
-    # steps 2-4 are read (each follows a whole step, as in the timed loop,
-    # rather than a host synchronisation); otherwise single eager steps.
-    samples = []
-    sampler = None
+    # The GEMM inside the step: with graphs, the events of the timed region's
+    # last S steps; otherwise events around the GEMM of single eager steps.
     if graph is not None:
-        err = ""
-        try:
-            smarks = [(torch.cuda.Event(enable_timing=True, external=True),
-                       torch.cuda.Event(enable_timing=True, external=True)) for _ in range(4)]
-            sampler = torch.cuda.CUDAGraph()
-            cs = torch.cuda.Stream()
-            cs.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(cs):
-                with torch.cuda.graph(sampler, stream=cs):
-                    for mk in smarks:
-                        out = step(A, Wt_sh, mk)
-            torch.cuda.current_stream().wait_stream(cs)
-            torch.cuda.synchronize()
-        except Exception as e:  # capture refused on this rank
-            sampler, err = None, str(e)
-        if _max_over_ranks([0.0 if sampler is not None else 1.0])[0] > 0:
-            sampler = None
-        else:
-            for _ in range(4):
-                sampler.replay()
-                torch.cuda.synchronize()
-                samples += [a.elapsed_time(b) for a, b in smarks[1:]]
-    if sampler is None:
+        samples = [a.elapsed_time(b) for a, b in marks]
+        gemm_from = (f"median of the CUDA-event pairs around the GEMM in the timed region's "
+                     f"last {S} steps (event record nodes of the replayed graph)")
+    else:
+        samples = []
         for _ in range(min(10, max(3, args.steps))):
-            if graph is not None:
-                graph.replay()
-            else:
-                marks = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                out = step(A, Wt_sh, marks)
+            mk = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            out = step(A, Wt_sh, mk)
             torch.cuda.synchronize()
-            samples.append(marks[0].elapsed_time(marks[1]))
+            samples.append(mk[0].elapsed_time(mk[1]))
+        gemm_from = f"median of {len(samples)} CUDA-event pairs around the GEMM of single steps"
     gemm_ms = statistics.median(samples)
-    gemm_from = (f"median of {len(samples)} CUDA-event pairs around the GEMM: steps 2-4 of a "
-                 "captured 4-step graph, replayed 4 times" if sampler is not None else
-                 f"median of {len(samples)} CUDA-event pairs around the GEMM of single steps")
     _barrier()
     ms, gemm_ms_max = _max_over_ranks([ms, gemm_ms])
     value = job_flops / (ms * 1e-3) / 1e12
@@ -612,9 +591,8 @@ def run_ours(args):
     if not args.no_parity:
         parity = headline_parity(A, Wt_sh, out, recipe) if not batch else None
     del out
-    if graph is not None:  # released before the process group (they hold NCCL calls)
+    if graph is not None:  # released before the process group (it holds NCCL calls)
         del graph
-        sampler = None
         torch.cuda.synchronize()
 
     # ---- end to end through the public API, host buffers
