@@ -1276,26 +1276,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + pbuf * kPartialCols + 128 * half;
-        // 32-column TMEM loads, one in flight while the previous one is
-        // promoted; the partial buffer is handed back once the last load has
-        // landed, before its FMAs. Packed FMAs (fma.rn.f32x2) round each
-        // element as one IEEE fma.
+        // 32-column TMEM loads issued in pairs (both in flight, one wait per
+        // pair: two load latencies per K block instead of four); the partial
+        // buffer is handed back once the second pair has landed, before its
+        // FMAs. Packed FMAs (fma.rn.f32x2) round each element as one IEEE fma.
         const float2 s2 = make_float2(s, s);
         uint32_t ra[32], rb[32];
-        tmem_ld32(taddr, ra);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-          tmem_ld_wait();
-          reg_bind32(cur);
-          if (c < 3) {
-            tmem_ld32(taddr + 32 * (c + 1), nxt);
-          } else {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pempty[pbuf]);
-          }
+        auto promote = [&](const uint32_t (&cur)[32], int c) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float2 v = __ffma2_rn(
@@ -1304,7 +1291,24 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             acc[32 * c + 2 * i] = v.x;
             acc[32 * c + 2 * i + 1] = v.y;
           }
-        }
+        };
+        tmem_ld32(taddr, ra);
+        tmem_ld32(taddr + 32, rb);
+        tmem_ld_wait();
+        reg_bind32(ra);
+        reg_bind32(rb);
+        promote(ra, 0);
+        promote(rb, 1);
+        tmem_ld32(taddr + 64, ra);
+        tmem_ld32(taddr + 96, rb);
+        tmem_ld_wait();
+        reg_bind32(ra);
+        reg_bind32(rb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[pbuf]);
+        promote(ra, 2);
+        promote(rb, 3);
         pbuf ^= 1;
         if (pbuf == 0) pphase ^= 1u;
       }
