@@ -167,7 +167,7 @@ template <int MT, int MODE>
 __device__ __forceinline__ void tile_math(float (&tot)[MT][4], const uint4 w0, const uint4 w1,
                                           const float2 sc, const float2 off,
                                           const __nv_bfloat16* const (&brow)[MT],
-                                          const bool (&brow_ok)[2], const float* sa_g, int t) {
+                                          const float* sa_g, int t) {
   const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w};
   const uint32_t r1[4] = {w1.x, w1.y, w1.z, w1.w};
   float acc[2][MT][4];
@@ -187,8 +187,7 @@ __device__ __forceinline__ void tile_math(float (&tot)[MT][4], const uint4 w0, c
                               code_pair<1>(u1)};
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        uint2 bv = make_uint2(0u, 0u);
-        if (brow_ok[mt]) bv = *reinterpret_cast<const uint2*>(brow[mt] + 8 * i + 4 * h);
+        const uint2 bv = *reinterpret_cast<const uint2*>(brow[mt] + 8 * i + 4 * h);
         if (i == 0) mma_bf16_first(acc[h][mt], af, bv.x, bv.y);
         else mma_bf16(acc[h][mt], af, bv.x, bv.y);
       }
@@ -385,7 +384,10 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
   // -------------------------------------------------------------- consumers
   const int gid = lane >> 2, t = lane & 3;
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-  const bool brow_ok[2] = {gid < p.M, 8 + gid < p.M};
+  // activation row of this lane's B fragments. Lanes past the last row read
+  // row M - 1 instead of zeros: they only feed output columns m >= M, which
+  // no path stores (and no guard or zeroing is needed per fragment).
+  const int arow[2] = {min(gid, p.M - 1), min(8 + gid, p.M - 1)};
   float tot[MT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -426,10 +428,8 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
         for (int kt = 0; kt < 8; ++kt) {
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            uint2 bv = make_uint2(0u, 0u);
-            if (brow_ok[mt])
-              bv = *reinterpret_cast<const uint2*>(As + (size_t)(mt * 8 + gid) * rs + g * G +
-                                                   32 * t + 4 * kt);
+            const uint2 bv = *reinterpret_cast<const uint2*>(As + (size_t)arow[mt] * rs + g * G +
+                                                             32 * t + 4 * kt);
             if (kt < 2) mma_bf16_first(s2[kt & 1][mt], ones, bv.x, bv.y);
             else mma_bf16(s2[kt & 1][mt], ones, bv.x, bv.y);
           }
@@ -477,8 +477,8 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
               const __nv_bfloat16* bg[MT];
 #pragma unroll
               for (int mt = 0; mt < MT; ++mt)
-                bg[mt] = As + (size_t)(mt * 8 + gid) * rs + 32 * t + j * G;
-              tile_math<MT, MODE>(own[o], w0, w1, sc, off, bg, brow_ok, SAs + j * 16, t);
+                bg[mt] = As + (size_t)arow[mt] * rs + 32 * t + j * G;
+              tile_math<MT, MODE>(own[o], w0, w1, sc, off, bg, SAs + j * 16, t);
             }
           }
         }
@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
 
     const __nv_bfloat16* brow[MT];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) brow[mt] = As + (size_t)(mt * 8 + gid) * rs + 32 * t;
+    for (int mt = 0; mt < MT; ++mt) brow[mt] = As + (size_t)arow[mt] * rs + 32 * t;
     // this warp's tiles of stage k: i = k * STAGE_TILES + TPW * warp + j, j < TPW,
     // consecutive groups of one row block (gpc is a multiple of 8)
     int rbl = TPW * warp / gpc, gl = TPW * warp - (TPW * warp / gpc) * gpc, cur_rbl = rbl;
@@ -542,8 +542,7 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
             const __nv_bfloat16* bg[MT];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) bg[mt] = brow[mt] + (gl + j) * G;
-            tile_math<MT, MODE>(tot, w0[j], w1[j], sc[j], off[j], bg, brow_ok,
-                                SAs + (gl + j) * 16, t);
+            tile_math<MT, MODE>(tot, w0[j], w1[j], sc[j], off[j], bg, SAs + (gl + j) * 16, t);
           }
         }
       }
