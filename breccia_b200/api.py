@@ -458,10 +458,11 @@ def matmul(a, b, out_dtype=np.float32, *, b_kmajor=False):
     return gemm.matmul(a, b, _torch_out_dtype(out_dtype), b_kmajor=b_kmajor)
 
 
-# Narrowest GEMM (output columns) for which cast_matmul picks the fused
-# kernel by itself: C2 (16384 x 8192 x 8192) measured fused 0.822 vs 0.835 ms
-# (delayed) and 0.864 vs 0.866 ms (current); at N = 4096 the fused launch took
-# 0.52-0.58 ms against 0.44-0.47 ms for cast then GEMM.
+# cast_matmul picks the fused kernel by itself only for a history-scaled cast
+# (one pass, no amax pass before the GEMM) and N >= _FUSED_MIN_N. At C2
+# (16384 x 8192 x 8192) it measured 0.810-0.830 against 0.815-0.835 ms for the
+# cast then the GEMM; with the current amax it measured 0.847-0.872 against
+# 0.846-0.857 ms; at N = 4096 it took 0.52-0.58 ms against 0.44-0.47 ms.
 _FUSED_MIN_N = 8192
 
 
@@ -480,10 +481,12 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
     and ``N % 16 == 0``: one GEMM launch whose extra warps encode ``x`` while
     the tensor cores work (only the first ``prologue_rows`` rows, ``-1`` = one
     tile group of 2048, are encoded before it). ``fused=None`` uses it where
-    it measured no slower than the separate cast on B200: ``N >= 8192`` (each
-    activation tile feeds at least 32 output tiles); below that the in-kernel
-    encode cannot keep up and ``cast`` then ``matmul`` runs. ``True`` / ``False``
-    force either way (``True`` still needs the shape conditions)."""
+    it measured no slower than the separate cast on B200: a DelayedScaling
+    cast from a recorded amax history with ``N >= 8192`` (each activation tile
+    feeds at least 32 output tiles). Otherwise ``cast`` then ``matmul`` runs:
+    with the current amax the separate passes measured as fast or faster, and
+    below ``N = 8192`` the in-kernel encode cannot keep up. ``True`` /
+    ``False`` force either way (``True`` still needs the shape conditions)."""
     from . import gemm
     x = _input(x)
     name = getattr(recipe, "name", None)
@@ -498,7 +501,8 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
         N, Kb = b.data.shape if b_kmajor else tuple(reversed(b.data.shape))
         ok = Kb == K and K > 0 and K % 128 == 0 and N % 16 == 0
         if ok and fused is None:
-            ok = N >= _FUSED_MIN_N
+            ok = (N >= _FUSED_MIN_N and amax_history is not None and
+                  amax_history.recorded > 0)
     if not ok or fused is False:
         a = cast(x, recipe, amax_history=amax_history)
         return matmul(a, b, out_dtype, b_kmajor=b_kmajor), a
