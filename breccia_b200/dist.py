@@ -190,13 +190,12 @@ def cast_matmul_weight_split(a, w_shard, recipe, group=None, out_dtype=torch.bfl
     followed by ``linear``.
 
     Every rank encodes the whole (replicated) activation while its GEMM
-    covers only ``1/world`` of the output columns. ``fused=None`` takes the
-    fused launch only where it measured no slower on B200 (a rank's N >=
-    8192, i.e. one rank); for narrower shards the in-kernel encode is the
-    slower way (N = 1024: 0.229 vs 0.169 ms for the apply pass + GEMM), so the
-    apply pass runs first. Per-tensor recipes only (others:
-    ``cast_weight_split`` + ``linear``)."""
-    from .api import _fused_cast_gemm, _torch_out_dtype, linear, _FUSED_MIN_N
+    covers only ``1/world`` of the output columns. On B200 the fused launch
+    measured slower than the apply pass + GEMM at every shard width (N = 1024:
+    0.441 vs 0.169 ms; N = 8192: 0.819 vs 0.809 ms), so ``fused=None`` runs the
+    apply pass first; ``fused=True`` takes the fused launch. Per-tensor
+    recipes only (others: ``cast_weight_split`` + ``linear``)."""
+    from .api import _fused_cast_gemm, _torch_out_dtype, linear
     if getattr(recipe, "name", None) not in ("delayed", "current"):
         sa, sw = cast_weight_split(a, w_shard, recipe, group)
         return linear(sa, sw, out_dtype), sa, sw
@@ -206,7 +205,7 @@ def cast_matmul_weight_split(a, w_shard, recipe, group=None, out_dtype=torch.bfl
     rows = x.numel() // K if K else 0
     N = w.shape[0]
     if fused is None:
-        fused = N >= _FUSED_MIN_N
+        fused = False  # the current-amax step measured no faster fused (cast_matmul)
     if not (fused and K > 0 and K % 128 == 0 and N % 16 == 0 and w.ndim == 2 and x.ndim >= 1):
         sa, sw = cast_weight_split(a, w_shard, recipe, group)
         return linear(sa, sw, out_dtype), sa, sw
