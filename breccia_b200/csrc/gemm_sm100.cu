@@ -1640,7 +1640,8 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
     to_pair_params(p);
     // 16 row blocks (4096 rows, a 33.5 MB A panel at K = 8192) per tile group:
     // C2's weight then streams from DRAM 4 times instead of 8 (748.7 -> 730.2
-    // us); the MXFP8 GEMM measured no better with it and keeps 8.
+    // us); 32 (a 67 MB panel that no longer stays in L2) measured 809 against
+    // 751 us, and the MXFP8 GEMM measured no better with 16 and keeps 8.
     p.group_m = kGroupM;
     p.a_scale = a_scale;
     p.b_scale = b_scale;
