@@ -460,9 +460,10 @@ def matmul(a, b, out_dtype=np.float32, *, b_kmajor=False):
 
 # cast_matmul picks the fused kernel by itself only for a history-scaled cast
 # (one pass, no amax pass before the GEMM) and N >= _FUSED_MIN_N. At C2
-# (16384 x 8192 x 8192) it measured 0.810-0.830 against 0.815-0.835 ms for the
-# cast then the GEMM; with the current amax it measured 0.847-0.872 against
-# 0.846-0.857 ms; at N = 4096 it took 0.52-0.58 ms against 0.44-0.47 ms.
+# (16384 x 8192 x 8192) it measured 0.809-0.811 against 0.817-0.825 ms for the
+# cast then the GEMM; with the current amax 0.847-0.854 against 0.851-0.859 ms
+# (level: the amax pass still runs first); at N = 4096 it took 0.52-0.58 ms
+# against 0.44-0.47 ms.
 _FUSED_MIN_N = 8192
 
 
@@ -480,7 +481,7 @@ def cast_matmul(x, b, recipe, *, amax_history: Optional[AmaxHistory] = None,
     ``Float8CurrentScaling``) and a 2-D per-tensor ``b`` with ``K % 128 == 0``
     and ``N % 16 == 0``: one GEMM launch whose extra warps encode ``x`` while
     the tensor cores work (only the first ``prologue_rows`` rows, ``-1`` = one
-    tile group of 2048, are encoded before it). ``fused=None`` uses it where
+    tile group of 4096, are encoded before it). ``fused=None`` uses it where
     it measured no slower than the separate cast on B200: a DelayedScaling
     cast from a recorded amax history with ``N >= 8192`` (each activation tile
     feeds at least 32 output tiles). Otherwise ``cast`` then ``matmul`` runs:

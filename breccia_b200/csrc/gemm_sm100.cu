@@ -1712,9 +1712,12 @@ int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uin
   }
   // 2. the first tile group's rows, before the GEMM (all of A when there is
   //    no GEMM to overlap with)
+  // tile groups of 16 row blocks, as the plain per-tensor GEMM: the first
+  // group's rows are encoded before the launch
+  const int group_m = kGroupM;
   int first = M;
   if (N > 0) {
-    const int group_rows = (kGroupM / 2) * P_BM;
+    const int group_rows = group_m * P_BM;
     first = prologue_rows < 0 ? group_rows : prologue_rows / P_BM * P_BM;
     if (first > M) first = M;
   }
@@ -1728,6 +1731,7 @@ int brc_cast_gemm_pertensor_fp8(const void* x, int x_dtype, int a_fmt, const uin
     if ((rc = make_tmap(&tb, b, N, K, 128))) return rc;
     Params p = base_params(M, N, K, BKB, d);
     to_pair_params(p);
+    p.group_m = group_m;
     p.a_scale = a_scale_out;
     p.b_scale = b_scale;
     p.status = status_word();

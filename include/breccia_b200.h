@@ -288,7 +288,7 @@ int brc_gemm_fp8_pertensor(const uint8_t* a, const uint8_t* b, int M, int N, int
  * x (M, K) float32 / bfloat16 / float16 is cast to a_fmt codes and
  *   D = (A_codes @ B_codes^T) * a_scale * b_scale
  * in one GEMM launch whose extra warps encode A while the tensor cores run;
- * only the first tile group's rows (prologue_rows, < 0 = 2048) are encoded
+ * only the first tile group's rows (prologue_rows, < 0 = 4096) are encoded
  * before it. Outputs equal brc_cast_pertensor_fp8 (history == NULL, or
  * use_history == 0) or brc_cast_pertensor_fp8_delayed (history, use_history)
  * followed by brc_gemm_fp8_pertensor, bit for bit: a_codes / a_scale_out are
