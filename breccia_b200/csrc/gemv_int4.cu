@@ -100,7 +100,7 @@ struct Params {
 };
 
 struct Layout {  // byte offsets into dynamic shared memory
-  uint32_t a, sa, acc, ring, full, empty, afull, aempty, misc, total;
+  uint32_t a, sa, acc, ring, full, empty, afull, aempty, safull, misc, total;
 };
 
 __host__ __device__ inline uint32_t take(uint32_t& o, uint32_t bytes) {
@@ -119,6 +119,7 @@ __host__ __device__ inline Layout layout(int NC, int M, int kc, int nb, int stag
   L.empty = take(o, (uint32_t)(stages * 8));
   L.afull = take(o, 2 * 8);
   L.aempty = take(o, 2 * 8);
+  L.safull = take(o, 2 * 8);
   L.misc = take(o, 16);
   L.total = o;
   return L;
@@ -246,6 +247,9 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
   uint64_t* afull = reinterpret_cast<uint64_t*>(smem + L.afull);
   uint64_t* aempty = reinterpret_cast<uint64_t*>(smem + L.aempty);
+  // a chunk buffer's activation group sums are in shared memory (one arrival
+  // per warp that computes some of them)
+  uint64_t* safull = reinterpret_cast<uint64_t*>(smem + L.safull);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc);
 
   if (threadIdx.x == 0) {
@@ -256,6 +260,7 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
     for (int b = 0; b < 2; ++b) {
       mbar_init(&afull[b], 1);
       mbar_init(&aempty[b], kConsumers);
+      mbar_init(&safull[b], min(p.kc / G, kConsumers));
     }
     *abort_flag = 0u;
     fence_mbar_init();
@@ -441,8 +446,17 @@ __global__ void __launch_bounds__(threads_for(NC), 1) k_int4_skinny(const Params
                 make_float2(s2[0][mt][0] + s2[1][mt][0], s2[0][mt][1] + s2[1][mt][1]);
         }
       }
+      if (warp < gpc) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&safull[b]);
+      }
     }
-    consumers_sync<NC>();  // the chunk's sums are visible
+    // The chunk's sums are visible once every warp that computes some has
+    // arrived. (An mbarrier rather than a barrier of all consumer warps: no
+    // warp waits for the others to finish the previous chunk. The sum buffer
+    // is free again when its activation buffer is refilled, which waits for
+    // every warp's "done" arrival on aempty.)
+    if (ok) ok = wait_or_abort(&safull[b], (uint32_t)((c / p.nb) & 1), abort_flag, p.status);
 
     if constexpr (OWNER) {
       const int rbs = STAGE_TILES / gpc;  // row blocks per stage
