@@ -1176,19 +1176,38 @@ __device__ __forceinline__ uint32_t enc4_fp8_from_f16x2(uint32_t h0, uint32_t h1
   return apply_sign8(w, neg);
 }
 
+// One thread per 32-element block. The next block's 34 input bytes are loaded
+// before the current block is encoded, so two blocks' loads are in flight per
+// thread (4 CTAs of 256 threads per SM: about 70 KB per SM).
 template <int FMT>
-__global__ void __launch_bounds__(256) k_requant_nv_to_mx(const uint8_t* __restrict__ codes,
-                                                          const uint8_t* __restrict__ scales,
-                                                          int64_t n_blocks, FastDiv bpr,
-                                                          uint32_t sf_col_tiles, uint8_t* out,
-                                                          uint8_t* out_scales,
-                                                          uint8_t* out_mma) {
+__global__ void __launch_bounds__(256, 4) k_requant_nv_to_mx(const uint8_t* __restrict__ codes,
+                                                             const uint8_t* __restrict__ scales,
+                                                             int64_t n_blocks, FastDiv bpr,
+                                                             uint32_t sf_col_tiles, uint8_t* out,
+                                                             uint8_t* out_scales,
+                                                             uint8_t* out_mma) {
   constexpr float kMax = FMT == BRC_FP8_E4M3 ? 448.f : 57344.f;
-  for (int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; blk < n_blocks;
-       blk += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 c0 = ldg16(codes + blk * 32), c1 = ldg16(codes + blk * 32 + 16);
-    const uint32_t hs0 = e4m3_to_f16x2_bcast(scales[2 * blk]);
-    const uint32_t hs1 = e4m3_to_f16x2_bcast(scales[2 * blk + 1]);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint4 n0 = make_uint4(0u, 0u, 0u, 0u), n1 = n0;
+  uint8_t ns0 = 0, ns1 = 0;
+  if (blk < n_blocks) {
+    n0 = ldg16(codes + blk * 32);
+    n1 = ldg16(codes + blk * 32 + 16);
+    ns0 = scales[2 * blk];
+    ns1 = scales[2 * blk + 1];
+  }
+  for (; blk < n_blocks; blk += stride) {
+    const uint4 c0 = n0, c1 = n1;
+    const uint32_t hs0 = e4m3_to_f16x2_bcast(ns0);
+    const uint32_t hs1 = e4m3_to_f16x2_bcast(ns1);
+    if (blk + stride < n_blocks) {
+      const int64_t nxt = blk + stride;
+      n0 = ldg16(codes + nxt * 32);
+      n1 = ldg16(codes + nxt * 32 + 16);
+      ns0 = scales[2 * nxt];
+      ns1 = scales[2 * nxt + 1];
+    }
     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     uint32_t h[16];  // f16x2 values (element 2i low, 2i+1 high)
     uint32_t amax2 = 0u;
@@ -2020,11 +2039,23 @@ __global__ void __launch_bounds__(256) k_delayed_apply(const void* __restrict__ 
       *reinterpret_cast<uint32_t*>(codes + vi * V) = w0[0];
     }
   };
+  // Four 16-byte vectors per iteration; the next iteration's four are loaded
+  // before this iteration's are encoded, so loads stay in flight while the
+  // thread computes.
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint4 nv[4];
+  if (i + 3 * stride < nvec) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) nv[u] = ldg16(base + 16 * (i + u * stride));
+  }
   for (; i + 3 * stride < nvec; i += 4 * stride) {
     uint4 v[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = ldg16(base + 16 * (i + u * stride));
+    for (int u = 0; u < 4; ++u) v[u] = nv[u];
+    if (i + 7 * stride < nvec) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nv[u] = ldg16(base + 16 * (i + (4 + u) * stride));
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u) encode_store(v[u], i + u * stride);
   }
