@@ -1287,8 +1287,9 @@ bool valid_out(int dt) { return valid_dtype(dt); }
 
 // Grid of a grid-stride kernel: one CTA per `per_cta` work items, at most
 // `per_sm` CTAs per SM. Measured on B200: 8 suits most casts; the per-tensor
-// cast_ste apply and the INT4 casts ran 7-8% faster at 32, while the others
-// ran 3-14% slower there (and slower still at one resident wave).
+// cast_ste apply and the INT4 casts ran 7-8% faster at 32 and dequantize
+// 10-14% faster, while the other casts ran 3-14% slower there (and slower
+// still at one resident wave) and requantize did not change.
 int grid_for(int64_t work_items, int per_cta, int per_sm = 8) {
   const int64_t want = (work_items + per_cta - 1) / per_cta;
   const int64_t cap = (int64_t)sm_count() * per_sm;
@@ -1670,7 +1671,7 @@ int brc_cast_ste_block(const void* x, int x_dtype, int64_t rows, int64_t cols, i
 namespace {
 template <int DQ, int FMT>
 int launch_dequant(const DequantArgs& a, int out_dtype, cudaStream_t st) {
-  const int grid = grid_for(a.n / 16 + 1, 256 * 2);
+  const int grid = grid_for(a.n / 16 + 1, 256 * 2, 32);
   const int64_t cpr = a.cols / 16, cpb = a.block_k / 16;
   if (a.n / 4 >= (1ll << 31) || cpr >= (1ll << 31)) {
     if (out_dtype == BRC_DTYPE_F32) k_dequant_wide<DQ, FMT, BRC_DTYPE_F32><<<grid, 256, 0, st>>>(a);
