@@ -44,8 +44,11 @@ struct DqtArgs {
   int scale_f16;
 };
 
+// Up to 32 CTAs per SM: measured on B200 against 8, the transposing
+// dequantize (8192 x 28672) ran 286 -> 259 us (MXFP8), 266 -> 241 us (NVFP4)
+// and the byte transpose 161 -> 147 us.
 int grid_tiles(int64_t tiles) {
-  const int64_t cap = (int64_t)sm_count() * 8;
+  const int64_t cap = (int64_t)sm_count() * 32;
   return (int)(tiles < cap ? (tiles < 1 ? 1 : tiles) : cap);
 }
 
