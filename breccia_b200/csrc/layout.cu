@@ -161,32 +161,40 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
 }
 
 // (rows, cols) bytes -> (cols, rows); rows % 16 == 0, cols % 16 == 0.
+// 128 x 128 tiles: every input row segment read and every output row segment
+// written is 128 contiguous bytes.
+constexpr int kTT = 128;
 __global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __restrict__ in,
                                                           int64_t rows, int64_t cols,
                                                           uint8_t* __restrict__ out) {
-  __shared__ uint8_t tile[kTile][kTile + 4];
-  const int64_t tiles_r = (rows + kTile - 1) / kTile;
-  const int64_t tiles_c = (cols + kTile - 1) / kTile;
-  const int lr = threadIdx.x >> 2, lc = (threadIdx.x & 3) * 16;
+  __shared__ __align__(16) uint8_t tile[kTT][kTT + 4];
+  const int64_t tiles_r = (rows + kTT - 1) / kTT;
+  const int64_t tiles_c = (cols + kTT - 1) / kTT;
+  const int lr = threadIdx.x >> 3, lc = (threadIdx.x & 7) * 16;  // 32 rows x 8 segments
   for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
-    const int64_t r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
-    const int64_t r = r0 + lr, c = c0 + lc;
-    uint4 cv = make_uint4(0u, 0u, 0u, 0u);
-    if (r < rows && c < cols) cv = ldg16(in + r * cols + c);
-    const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
+    const int64_t r0 = (t / tiles_c) * kTT, c0 = (t % tiles_c) * kTT;
+    uint4 cv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int64_t r = r0 + lr + 32 * q, c = c0 + lc;
+      cv[q] = (r < rows && c < cols) ? ldg16(in + r * cols + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads();  // the previous tile's readers are done with `tile`
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w[4] = {cv[q].x, cv[q].y, cv[q].z, cv[q].w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        tile[lc + i][lr + 32 * q] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+    }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) tile[lc + i][lr] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
-    __syncthreads();
-    const int64_t oc = c0 + lr, orow = r0 + lc;
-    if (oc < cols && orow < rows) {
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = (uint32_t)tile[lr][lc + 4 * j] | ((uint32_t)tile[lr][lc + 4 * j + 1] << 8) |
-               ((uint32_t)tile[lr][lc + 4 * j + 2] << 16) |
-               ((uint32_t)tile[lr][lc + 4 * j + 3] << 24);
-      stg16(out + oc * rows + orow, make_uint4(o[0], o[1], o[2], o[3]));
+    for (int q = 0; q < 4; ++q) {
+      const int64_t oc = c0 + lr + 32 * q, orow = r0 + lc;
+      if (oc < cols && orow < rows) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&tile[lr + 32 * q][lc]);
+        stg16(out + oc * rows + orow, make_uint4(src[0], src[1], src[2], src[3]));
+      }
     }
   }
 }
@@ -265,7 +273,7 @@ int brc_transpose_u8(const uint8_t* in, int64_t rows, int64_t cols, uint8_t* out
   if ((!in || !out) && rows * cols > 0) return BRC_ERR_NULL;
   if (rows * cols == 0) return BRC_OK;
   if (!aligned16(in) || !aligned16(out)) return BRC_ERR_ALIGN;
-  const int64_t tiles = ((rows + kTile - 1) / kTile) * ((cols + kTile - 1) / kTile);
+  const int64_t tiles = ((rows + kTT - 1) / kTT) * ((cols + kTT - 1) / kTT);
   k_transpose_u8<<<grid_tiles(tiles), kThreads, 0, (cudaStream_t)stream>>>(in, rows, cols, out);
   return check_launch();
 }
