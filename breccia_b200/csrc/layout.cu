@@ -162,38 +162,52 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
 
 // (rows, cols) bytes -> (cols, rows); rows % 16 == 0, cols % 16 == 0.
 // 128 x 128 tiles: every input row segment read and every output row segment
-// written is 128 contiguous bytes.
+// written is 128 contiguous bytes. Thread (a, b) loads rows 4a..4a+3 of the
+// 16-byte column group b and transposes each 4 x 4 byte block in registers
+// (byte permutes), so shared memory sees whole 32-bit words: word a of output
+// row R (input rows 4a..4a+3 of column R) sits at a ^ 4 * (R / 16), which puts
+// a warp's 32 stores and each quarter-warp's 16-byte reads in distinct banks.
 constexpr int kTT = 128;
+__device__ __forceinline__ uint32_t prmt_u32(uint32_t x, uint32_t y, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(y), "r"(sel));
+  return d;
+}
 __global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __restrict__ in,
                                                           int64_t rows, int64_t cols,
                                                           uint8_t* __restrict__ out) {
-  __shared__ __align__(16) uint8_t tile[kTT][kTT + 4];
+  __shared__ __align__(16) uint32_t tile[kTT][kTT / 4];
   const int64_t tiles_r = (rows + kTT - 1) / kTT;
   const int64_t tiles_c = (cols + kTT - 1) / kTT;
-  const int lr = threadIdx.x >> 3, lc = (threadIdx.x & 7) * 16;  // 32 rows x 8 segments
+  const int a = threadIdx.x >> 3, b = threadIdx.x & 7;  // load: 4-row group, column group
   for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
     const int64_t r0 = (t / tiles_c) * kTT, c0 = (t % tiles_c) * kTT;
-    uint4 cv[4];
+    uint4 v[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int64_t r = r0 + lr + 32 * q, c = c0 + lc;
-      cv[q] = (r < rows && c < cols) ? ldg16(in + r * cols + c) : make_uint4(0u, 0u, 0u, 0u);
+    for (int k = 0; k < 4; ++k) {
+      const int64_t r = r0 + 4 * a + k, c = c0 + 16 * b;
+      v[k] = (r < rows && c < cols) ? ldg16(in + r * cols + c) : make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();  // the previous tile's readers are done with `tile`
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w[4] = {cv[q].x, cv[q].y, cv[q].z, cv[q].w};
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t x0 = (&v[0].x)[j], x1 = (&v[1].x)[j], x2 = (&v[2].x)[j],
+                     x3 = (&v[3].x)[j];
+      const uint32_t t0 = prmt_u32(x0, x1, 0x5140u), t1 = prmt_u32(x0, x1, 0x7362u);
+      const uint32_t t2 = prmt_u32(x2, x3, 0x5140u), t3 = prmt_u32(x2, x3, 0x7362u);
+      const uint32_t o[4] = {prmt_u32(t0, t2, 0x5410u), prmt_u32(t0, t2, 0x7632u),
+                             prmt_u32(t1, t3, 0x5410u), prmt_u32(t1, t3, 0x7632u)};
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        tile[lc + i][lr + 32 * q] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+      for (int m = 0; m < 4; ++m) tile[16 * b + 4 * j + m][a ^ (b << 2)] = o[m];
     }
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int64_t oc = c0 + lr + 32 * q, orow = r0 + lc;
+      const int R = 32 * q + (threadIdx.x >> 3), sg = threadIdx.x & 7;
+      const int64_t oc = c0 + R, orow = r0 + 16 * sg;
       if (oc < cols && orow < rows) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(&tile[lr + 32 * q][lc]);
-        stg16(out + oc * rows + orow, make_uint4(src[0], src[1], src[2], src[3]));
+        const uint4 w = *reinterpret_cast<const uint4*>(&tile[R][(sg ^ (R >> 4)) * 4]);
+        stg16(out + oc * rows + orow, w);
       }
     }
   }
