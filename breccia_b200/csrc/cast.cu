@@ -136,33 +136,6 @@ struct LaneVals {
 // x + (y - x) in float32, as the reference's x + (y - x).detach() evaluates it.
 // The values go straight to this lane's slot of the warp's shared-memory
 // stage (16 bytes at a time), so no register array holds them.
-// FP8 pairs to f16 pairs by the hardware conversion: every E4M3 / E5M2 value
-// (subnormals, infinities and NaN included) is exact in float16 and again in
-// float32, so the float32 product below rounds exactly once, as the
-// reference's decode-then-multiply does. Byte i of the pair lands in half i.
-template <int FMT>
-__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
-  uint32_t d;
-  const uint16_t b = (uint16_t)two;
-  if constexpr (FMT == BRC_FP8_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(b));
-  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(b));
-  return d;
-}
-// Two E2M1 codes (one per byte, low nibbles) to f16 pairs, exactly.
-__device__ __forceinline__ uint32_t e2m1_bytes_to_f16x2(uint32_t two) {
-  uint32_t d;
-  const uint32_t pair = (two & 0x0Fu) | ((two >> 4) & 0xF0u);
-  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
-      : "=r"(d)
-      : "r"(pair));
-  return d;
-}
-__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
-  const __half2 v = *reinterpret_cast<const __half2*>(&h);
-  lo = __low2float(v);
-  hi = __high2float(v);
-}
-
 template <int MODE, int FMT, int NW>
 __device__ __forceinline__ void ste_values(const BlockCastArgs& a, const float* f,
                                            const uint32_t* w, float dqs, float dqz, float* o) {

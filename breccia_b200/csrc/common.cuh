@@ -355,6 +355,33 @@ __device__ __forceinline__ float dec_fp8(uint32_t c) {
   else return dec_e5m2(c);
 }
 
+// FP8 pairs to f16 pairs by the hardware conversion: every E4M3 / E5M2 value
+// (subnormals, infinities and NaN included) is exact in float16 and again in
+// float32, so a float32 product of the decoded value rounds exactly once, as
+// the reference's decode-then-multiply does. Byte i of the pair lands in half i.
+template <int FMT>
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint16_t b = (uint16_t)two;
+  if constexpr (FMT == BRC_FP8_E4M3) asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(b));
+  else asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(b));
+  return d;
+}
+// Two E2M1 codes (one per byte, low nibbles) to f16 pairs, exactly.
+__device__ __forceinline__ uint32_t e2m1_bytes_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint32_t pair = (two & 0x0Fu) | ((two >> 4) & 0xF0u);
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(d)
+      : "r"(pair));
+  return d;
+}
+__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
+  const __half2 v = *reinterpret_cast<const __half2*>(&h);
+  lo = __low2float(v);
+  hi = __high2float(v);
+}
+
 // ------------------------------------------------------------ E8M0
 // E8M0 exponent of a float32 scale exactly as numpy computes
 // round(log2(max(s, 1e-10f))) + 127 clipped to [0, 255]

@@ -14,10 +14,12 @@
 //   k_transpose_u8 (rows, cols) bytes -> (cols, rows): per-tensor FP8 codes do
 //                  not depend on orientation, so they move as plain bytes.
 //
-// Both stage 64 x 64 tiles through shared memory: every thread loads 16
-// consecutive elements of one source row (16-byte loads) and stores 16
-// consecutive elements of one destination row, so global traffic stays
-// coalesced in both orientations.
+// Both stage 128 x 128 tiles of codes through shared memory as transposed
+// bytes: a thread loads 16 consecutive codes of each of 4 source rows
+// (16-byte loads, 128 contiguous bytes per row per warp), transposes the 4 x 4
+// byte blocks in registers and stores whole 32-bit words; destination rows are
+// written in 16-byte pieces, so global traffic stays coalesced in both
+// orientations.
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -29,7 +31,6 @@
 namespace brc {
 namespace {
 
-constexpr int kTile = 64;
 constexpr int kThreads = 256;
 
 struct DqtArgs {
@@ -81,82 +82,6 @@ __device__ __forceinline__ void store8(void* out, int64_t e0, const float* v) {
       }
     }
     stg16(static_cast<char*>(out) + e0 * 2, make_uint4(w[0], w[1], w[2], w[3]));
-  }
-}
-
-// KIND: BRC_STE_BLOCK_FP8, BRC_STE_MXFP8, BRC_STE_NVFP4, BRC_STE_INT4 or
-// BRC_KIND_PERTENSOR_FP8. rows % 8 == 0, cols % 16 == 0, block % 16 == 0.
-template <int KIND, int FMT, int OUT>
-__global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
-  __shared__ float tile[kTile][kTile + 1];
-  const int64_t tiles_r = (a.rows + kTile - 1) / kTile;
-  const int64_t tiles_c = (a.cols + kTile - 1) / kTile;
-  const int lr = threadIdx.x >> 2;          // tile row this thread loads / column it stores
-  const int lc = (threadIdx.x & 3) * 16;    // 16-element segment
-  for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
-    const int64_t r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
-    const int64_t r = r0 + lr, c = c0 + lc;
-    float v[16];
-    if (r < a.rows && c < a.cols) {
-      const uint4 cv = ldg16(a.codes + r * a.cols + c);
-      const uint32_t w[4] = {cv.x, cv.y, cv.z, cv.w};
-      float scale = 0.f, zp = 0.f;
-      if constexpr (KIND == BRC_KIND_PERTENSOR_FP8) {
-        scale = *static_cast<const float*>(a.scales);
-      } else {
-        const int64_t si = r * a.scale_cols + c / a.block;
-        if constexpr (KIND == BRC_STE_BLOCK_FP8) {
-          scale = static_cast<const float*>(a.scales)[si];
-        } else if constexpr (KIND == BRC_STE_MXFP8) {
-          scale = e8m0_value(static_cast<const uint8_t*>(a.scales)[si]);
-        } else if constexpr (KIND == BRC_STE_NVFP4) {
-          scale = dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
-        } else {
-          if (a.scale_f16) {
-            scale = __half2float(static_cast<const __half*>(a.scales)[si]);
-            if (a.zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
-          } else {
-            scale = static_cast<const float*>(a.scales)[si];
-            if (a.zp) zp = static_cast<const float*>(a.zp)[si];
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t code = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-        float d;
-        if constexpr (KIND == BRC_STE_NVFP4) {
-          d = dec_e2m1(code);
-        } else if constexpr (KIND == BRC_STE_INT4) {
-          const uint32_t lo = code & 0xFu;
-          d = (a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
-          if (a.zp) d = __fsub_rn(d, zp);
-        } else {
-          d = dec_fp8<FMT>(code);
-        }
-        v[i] = __fmul_rn(d, scale);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-    }
-    __syncthreads();  // the previous tile's readers are done with `tile`
-#pragma unroll
-    for (int i = 0; i < 16; ++i) tile[lc + i][lr] = v[i];
-    __syncthreads();
-    const int64_t oc = c0 + lr;  // destination row (a source column)
-    if (oc < a.cols) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int64_t orow = r0 + lc + 8 * h;  // first source row of these 8
-        if (orow < a.rows) {
-          float w8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) w8[i] = tile[lr][lc + 8 * h + i];
-          store8<OUT>(a.out, oc * a.rows + orow, w8);
-        }
-      }
-    }
   }
 }
 
@@ -213,9 +138,126 @@ __global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __rest
   }
 }
 
+// KIND: BRC_STE_BLOCK_FP8, BRC_STE_MXFP8, BRC_STE_NVFP4, BRC_STE_INT4 or
+// BRC_KIND_PERTENSOR_FP8. rows % 8 == 0, cols % 16 == 0, block % 16 == 0,
+// cols % block == 0. One 128 x 128 tile of codes per iteration: the codes are
+// transposed as bytes (as in k_transpose_u8), the tile's scales (and zero
+// points) are decoded once into a table of [column block][row], and each
+// thread then decodes 8 codes of one output row (8 consecutive source rows of
+// one source column) with their 8 scales and stores 8 output values.
+constexpr int kDqtMaxCb = kTT / 16 + 1;  // column blocks a tile can touch
+template <int KIND, int FMT, int OUT>
+__global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
+  constexpr bool kTable = KIND != BRC_KIND_PERTENSOR_FP8;
+  constexpr bool kZp = KIND == BRC_STE_INT4;
+  __shared__ __align__(16) uint32_t ctile[kTT][kTT / 4];
+  __shared__ __align__(16) float sc[kTable ? kDqtMaxCb : 1][kTT];
+  __shared__ __align__(16) float zpt[kZp ? kDqtMaxCb : 1][kTT];
+  const int64_t tiles_r = (a.rows + kTT - 1) / kTT;
+  const int64_t tiles_c = (a.cols + kTT - 1) / kTT;
+  const int la = threadIdx.x >> 3, lb = threadIdx.x & 7;  // load: 4-row group, column group
+  float pt_scale = 0.f;
+  if constexpr (!kTable) pt_scale = *static_cast<const float*>(a.scales);
+  for (int64_t t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
+    const int64_t r0 = (t / tiles_c) * kTT, c0 = (t % tiles_c) * kTT;
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t r = r0 + 4 * la + k, c = c0 + 16 * lb;
+      v[k] = (r < a.rows && c < a.cols) ? ldg16(a.codes + r * a.cols + c)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+    const int64_t cb0 = c0 / a.block;
+    const int ncb = kTable ? (int)((min(c0 + kTT, a.cols) - 1) / a.block - cb0 + 1) : 0;
+    __syncthreads();  // the previous tile's readers are done with the shared tables
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t x0 = (&v[0].x)[j], x1 = (&v[1].x)[j], x2 = (&v[2].x)[j],
+                     x3 = (&v[3].x)[j];
+      const uint32_t t0 = prmt_u32(x0, x1, 0x5140u), t1 = prmt_u32(x0, x1, 0x7362u);
+      const uint32_t t2 = prmt_u32(x2, x3, 0x5140u), t3 = prmt_u32(x2, x3, 0x7362u);
+      const uint32_t o[4] = {prmt_u32(t0, t2, 0x5410u), prmt_u32(t0, t2, 0x7632u),
+                             prmt_u32(t1, t3, 0x5410u), prmt_u32(t1, t3, 0x7632u)};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) ctile[16 * lb + 4 * j + m][la ^ (lb << 2)] = o[m];
+    }
+    if constexpr (kTable) {
+      for (int e = threadIdx.x; e < ncb * kTT; e += kThreads) {
+        const int cbi = e % ncb, r = e / ncb;
+        float scale = 0.f, zp = 0.f;
+        if (r0 + r < a.rows) {
+          const int64_t si = (r0 + r) * a.scale_cols + cb0 + cbi;
+          if constexpr (KIND == BRC_STE_BLOCK_FP8) {
+            scale = static_cast<const float*>(a.scales)[si];
+          } else if constexpr (KIND == BRC_STE_MXFP8) {
+            scale = e8m0_value(static_cast<const uint8_t*>(a.scales)[si]);
+          } else if constexpr (KIND == BRC_STE_NVFP4) {
+            scale = dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
+          } else if (a.scale_f16) {
+            scale = __half2float(static_cast<const __half*>(a.scales)[si]);
+            if (a.zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
+          } else {
+            scale = static_cast<const float*>(a.scales)[si];
+            if (a.zp) zp = static_cast<const float*>(a.zp)[si];
+          }
+        }
+        sc[cbi][r] = scale;
+        if constexpr (kZp) zpt[cbi][r] = zp;
+      }
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int q = 0; q < 8; ++q) {
+      const int R = 16 * q + (threadIdx.x >> 4), sg = threadIdx.x & 15;  // output row, 8-row segment
+      const int64_t c = c0 + R, orow = r0 + 8 * sg;
+      if (c >= a.cols || orow >= a.rows) continue;
+      const uint2 w = *reinterpret_cast<const uint2*>(&ctile[R][(2 * sg) ^ ((R >> 4) << 2)]);
+      float s8[8], z8[8];
+      if constexpr (kTable) {
+        const int cbi = (int)(c / a.block - cb0);
+        const float4 sa = *reinterpret_cast<const float4*>(&sc[cbi][8 * sg]);
+        const float4 sb = *reinterpret_cast<const float4*>(&sc[cbi][8 * sg + 4]);
+        s8[0] = sa.x; s8[1] = sa.y; s8[2] = sa.z; s8[3] = sa.w;
+        s8[4] = sb.x; s8[5] = sb.y; s8[6] = sb.z; s8[7] = sb.w;
+        if constexpr (kZp) {
+          const float4 za = *reinterpret_cast<const float4*>(&zpt[cbi][8 * sg]);
+          const float4 zb = *reinterpret_cast<const float4*>(&zpt[cbi][8 * sg + 4]);
+          z8[0] = za.x; z8[1] = za.y; z8[2] = za.z; z8[3] = za.w;
+          z8[4] = zb.x; z8[5] = zb.y; z8[6] = zb.z; z8[7] = zb.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s8[i] = pt_scale;
+      }
+      float d8[8], o8[8];
+      if constexpr (KIND == BRC_STE_INT4) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t lo = ((i < 4 ? w.x : w.y) >> (8 * (i & 3))) & 0xFu;
+          d8[i] = (a.is_signed && lo >= 8) ? (float)((int)lo - 16) : (float)lo;
+          if (a.zp) d8[i] = __fsub_rn(d8[i], z8[i]);
+        }
+      } else {
+        // code pairs through the exact hardware conversions to f16
+        const uint32_t pr[4] = {w.x, w.x >> 16, w.y, w.y >> 16};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if constexpr (KIND == BRC_STE_NVFP4)
+            f16x2_to_f32(e2m1_bytes_to_f16x2(pr[k]), d8[2 * k], d8[2 * k + 1]);
+          else
+            f16x2_to_f32(fp8x2_to_f16x2<FMT>(pr[k]), d8[2 * k], d8[2 * k + 1]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = __fmul_rn(d8[i], s8[i]);
+      store8<OUT>(a.out, c * a.rows + orow, o8);
+    }
+  }
+}
+
 template <int KIND, int FMT>
 int launch_dqt(const DqtArgs& a, int out_dtype, cudaStream_t st) {
-  const int64_t tiles = ((a.rows + kTile - 1) / kTile) * ((a.cols + kTile - 1) / kTile);
+  const int64_t tiles = ((a.rows + kTT - 1) / kTT) * ((a.cols + kTT - 1) / kTT);
   const int grid = grid_tiles(tiles);
   if (out_dtype == BRC_DTYPE_F32)
     k_dequant_t<KIND, FMT, BRC_DTYPE_F32><<<grid, kThreads, 0, st>>>(a);

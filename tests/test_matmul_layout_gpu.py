@@ -80,14 +80,11 @@ def no_torch_fallback(monkeypatch):
     monkeypatch.setattr(gemm, "_general", refuse)
 
 
-@pytest.mark.parametrize("rname", list(_recipes()))
-@pytest.mark.parametrize("out", ["f32", "bf16"])
-def test_dequant_transposed_vs_oracle(rname, out):
+def _check_dequant_transposed(r, rows, cols, out, seed):
     from oracle import cast as ocast
     from breccia_b200 import _lib, gemm
-    r = _recipes()[rname]
-    g = torch.Generator().manual_seed(len(rname))
-    x = torch.randn(200, 384, generator=g) * 0.3
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, cols, generator=g) * 0.3
     x[3, :40] = 0.0
     x[7, 5] = 80.0
     st = bb().cast(x.cuda(), r)
@@ -100,9 +97,9 @@ def test_dequant_transposed_vs_oracle(rname, out):
         sdt = _lib.SCALE_F32
     zp = None if st.zero_point is None else st.zero_point.to(scale.dtype).contiguous()
     odt = torch.float32 if out == "f32" else torch.bfloat16
-    got = torch.empty((384, 200), dtype=odt, device="cuda")
-    _lib.call("brc_dequant_transposed", st.data.view(torch.uint8).data_ptr(), 200, 384, kind, fmt,
-              block, signed, sdt, scale.data_ptr(), None if zp is None else zp.data_ptr(),
+    got = torch.empty((cols, rows), dtype=odt, device="cuda")
+    _lib.call("brc_dequant_transposed", st.data.view(torch.uint8).data_ptr(), rows, cols, kind,
+              fmt, block, signed, sdt, scale.data_ptr(), None if zp is None else zp.data_ptr(),
               got.data_ptr(), _lib.DTYPE_F32 if out == "f32" else _lib.DTYPE_BF16,
               torch.cuda.current_stream().cuda_stream)
     g_np = got.float().cpu().numpy()
@@ -111,6 +108,30 @@ def test_dequant_transposed_vs_oracle(rname, out):
     else:
         ref_bf = torch.from_numpy(want).to(torch.bfloat16).float().numpy()
         assert same_bits(np.nan_to_num(g_np, nan=1234.5), np.nan_to_num(ref_bf, nan=1234.5))
+
+
+@pytest.mark.parametrize("rname", list(_recipes()))
+@pytest.mark.parametrize("out", ["f32", "bf16"])
+def test_dequant_transposed_vs_oracle(rname, out):
+    _check_dequant_transposed(_recipes()[rname], 200, 384, out, len(rname))
+
+
+@pytest.mark.parametrize("rname,rows,cols", [
+    ("block48", 136, 480),    # 48-wide blocks straddle the 128-column tiles
+    ("int4_g48", 264, 384),
+    ("mxfp8", 392, 640),      # several tiles each way, a partial last row tile
+    ("nvfp4", 8, 1040),
+    ("pertensor", 520, 144),
+])
+def test_dequant_transposed_tiles(rname, rows, cols):
+    from breccia_b200.types import (Float8CurrentScaling, Float8BlockScaling, MXFP8BlockScaling,
+                                    NVFP4BlockScaling, INT4Scaling)
+    r = {"block48": Float8BlockScaling(block_k=48),
+         "int4_g48": INT4Scaling(group_size=48, signed=False, symmetric=False),
+         "mxfp8": MXFP8BlockScaling(), "nvfp4": NVFP4BlockScaling(),
+         "pertensor": Float8CurrentScaling()}[rname]
+    for out in ("f32", "bf16"):
+        _check_dequant_transposed(r, rows, cols, out, rows + cols)
 
 
 def test_transpose_u8():
