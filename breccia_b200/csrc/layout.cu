@@ -182,8 +182,9 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
       for (int m = 0; m < 4; ++m) ctile[16 * lb + 4 * j + m][la ^ (lb << 2)] = o[m];
     }
     if constexpr (kTable) {
-      for (int e = threadIdx.x; e < ncb * kTT; e += kThreads) {
-        const int cbi = e % ncb, r = e / ncb;
+      // thread: one tile row, every (kThreads / kTT)-th column block
+      const int r = threadIdx.x & (kTT - 1);
+      for (int cbi = threadIdx.x / kTT; cbi < ncb; cbi += kThreads / kTT) {
         float scale = 0.f, zp = 0.f;
         if (r0 + r < a.rows) {
           const int64_t si = (r0 + r) * a.scale_cols + cb0 + cbi;
