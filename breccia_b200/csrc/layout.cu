@@ -169,6 +169,36 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
     }
     const int64_t cb0 = c0 / a.block;
     const int ncb = kTable ? (int)((min(c0 + kTT, a.cols) - 1) / a.block - cb0 + 1) : 0;
+    // Table entries of this thread (one tile row, every (kThreads / kTT)-th
+    // column block): their raw scale / zero-point bits are loaded here, beside
+    // the codes, so the two global loads overlap; decoded after the barrier.
+    constexpr int kPer = (kDqtMaxCb + kThreads / kTT - 1) / (kThreads / kTT);
+    const int r = threadIdx.x & (kTT - 1);
+    uint32_t sraw[kTable ? kPer : 1], zraw[kZp ? kPer : 1];
+    if constexpr (kTable) {
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int cbi = threadIdx.x / kTT + u * (kThreads / kTT);
+        sraw[u] = 0u;
+        if constexpr (kZp) zraw[u] = 0u;
+        if (cbi < ncb && r0 + r < a.rows) {
+          const int64_t si = (r0 + r) * a.scale_cols + cb0 + cbi;
+          if constexpr (KIND == BRC_STE_BLOCK_FP8) {
+            sraw[u] = __float_as_uint(static_cast<const float*>(a.scales)[si]);
+          } else if constexpr (KIND == BRC_STE_MXFP8 || KIND == BRC_STE_NVFP4) {
+            sraw[u] = static_cast<const uint8_t*>(a.scales)[si];
+          } else if (a.scale_f16) {
+            sraw[u] = __half_as_ushort(static_cast<const __half*>(a.scales)[si]);
+            if constexpr (kZp)
+              if (a.zp) zraw[u] = __half_as_ushort(static_cast<const __half*>(a.zp)[si]);
+          } else {
+            sraw[u] = __float_as_uint(static_cast<const float*>(a.scales)[si]);
+            if constexpr (kZp)
+              if (a.zp) zraw[u] = __float_as_uint(static_cast<const float*>(a.zp)[si]);
+          }
+        }
+      }
+    }
     __syncthreads();  // the previous tile's readers are done with the shared tables
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -182,28 +212,27 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
       for (int m = 0; m < 4; ++m) ctile[16 * lb + 4 * j + m][la ^ (lb << 2)] = o[m];
     }
     if constexpr (kTable) {
-      // thread: one tile row, every (kThreads / kTT)-th column block
-      const int r = threadIdx.x & (kTT - 1);
-      for (int cbi = threadIdx.x / kTT; cbi < ncb; cbi += kThreads / kTT) {
-        float scale = 0.f, zp = 0.f;
-        if (r0 + r < a.rows) {
-          const int64_t si = (r0 + r) * a.scale_cols + cb0 + cbi;
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int cbi = threadIdx.x / kTT + u * (kThreads / kTT);
+        if (cbi < ncb) {
+          float scale, zp = 0.f;
           if constexpr (KIND == BRC_STE_BLOCK_FP8) {
-            scale = static_cast<const float*>(a.scales)[si];
+            scale = __uint_as_float(sraw[u]);
           } else if constexpr (KIND == BRC_STE_MXFP8) {
-            scale = e8m0_value(static_cast<const uint8_t*>(a.scales)[si]);
+            scale = e8m0_value(sraw[u]);
           } else if constexpr (KIND == BRC_STE_NVFP4) {
-            scale = dec_e4m3(static_cast<const uint8_t*>(a.scales)[si]);
+            scale = dec_e4m3(sraw[u]);
           } else if (a.scale_f16) {
-            scale = __half2float(static_cast<const __half*>(a.scales)[si]);
-            if (a.zp) zp = __half2float(static_cast<const __half*>(a.zp)[si]);
+            scale = __half2float(__ushort_as_half((unsigned short)sraw[u]));
+            if constexpr (kZp) zp = __half2float(__ushort_as_half((unsigned short)zraw[u]));
           } else {
-            scale = static_cast<const float*>(a.scales)[si];
-            if (a.zp) zp = static_cast<const float*>(a.zp)[si];
+            scale = __uint_as_float(sraw[u]);
+            if constexpr (kZp) zp = __uint_as_float(zraw[u]);
           }
+          sc[cbi][r] = scale;
+          if constexpr (kZp) zpt[cbi][r] = zp;
         }
-        sc[cbi][r] = scale;
-        if constexpr (kZp) zpt[cbi][r] = zp;
       }
     }
     __syncthreads();
