@@ -1195,6 +1195,8 @@ NCU_CASES = {
     "dequant_mxfp8": "MXFP8 dequantize to f32, 8192x8192",
     "unpack_nvfp4": "packed 4-bit load (breccia's nibble order) -> codes + tensor-core packed "
                     "order, 16384x16384",
+    "layout_t": "breccia-orientation (K, N) operands, 8192x8192: MXFP8 transposing dequantize "
+                "to bf16, then the byte transpose of per-tensor FP8 codes",
 }
 
 
@@ -1238,6 +1240,16 @@ def run_ncu_case(name):
         lo = torch.empty(n // 2, dtype=torch.uint8, device=dev)
         fn = lambda: L.call("brc_unpack_nibbles_hi", pk.data_ptr(), n, codes.data_ptr(),  # noqa: E731
                             lo.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    elif name == "layout_t":
+        from breccia_b200 import _lib as L, gemm
+        st = bb.cast(bf16(8192, 8192, 0.02), bb.MXFP8BlockScaling())
+        codes = bb.cast(bf16(8192, 8192, 0.02), bb.Float8CurrentScaling()).data.view(torch.uint8)
+        out = torch.empty((8192, 8192), dtype=torch.uint8, device=dev)
+
+        def fn():
+            gemm._bf16_nk(st)
+            L.call("brc_transpose_u8", codes.data_ptr(), 8192, 8192, out.data_ptr(),
+                   torch.cuda.current_stream().cuda_stream)
     else:
         x, r, kw = {
             "cast_pertensor": (lambda: bf16(16384, 8192), bb.Float8CurrentScaling(), {}),
