@@ -93,11 +93,6 @@ __device__ __forceinline__ void store8(void* out, int64_t e0, const float* v) {
 // row R (input rows 4a..4a+3 of column R) sits at a ^ 4 * (R / 16), which puts
 // a warp's 32 stores and each quarter-warp's 16-byte reads in distinct banks.
 constexpr int kTT = 128;
-__device__ __forceinline__ uint32_t prmt_u32(uint32_t x, uint32_t y, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(y), "r"(sel));
-  return d;
-}
 __global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __restrict__ in,
                                                           int64_t rows, int64_t cols,
                                                           uint8_t* __restrict__ out) {
@@ -118,10 +113,10 @@ __global__ void __launch_bounds__(kThreads) k_transpose_u8(const uint8_t* __rest
     for (int j = 0; j < 4; ++j) {
       const uint32_t x0 = (&v[0].x)[j], x1 = (&v[1].x)[j], x2 = (&v[2].x)[j],
                      x3 = (&v[3].x)[j];
-      const uint32_t t0 = prmt_u32(x0, x1, 0x5140u), t1 = prmt_u32(x0, x1, 0x7362u);
-      const uint32_t t2 = prmt_u32(x2, x3, 0x5140u), t3 = prmt_u32(x2, x3, 0x7362u);
-      const uint32_t o[4] = {prmt_u32(t0, t2, 0x5410u), prmt_u32(t0, t2, 0x7632u),
-                             prmt_u32(t1, t3, 0x5410u), prmt_u32(t1, t3, 0x7632u)};
+      const uint32_t t0 = prmt(x0, x1, 0x5140u), t1 = prmt(x0, x1, 0x7362u);
+      const uint32_t t2 = prmt(x2, x3, 0x5140u), t3 = prmt(x2, x3, 0x7362u);
+      const uint32_t o[4] = {prmt(t0, t2, 0x5410u), prmt(t0, t2, 0x7632u),
+                             prmt(t1, t3, 0x5410u), prmt(t1, t3, 0x7632u)};
 #pragma unroll
       for (int m = 0; m < 4; ++m) tile[16 * b + 4 * j + m][a ^ (b << 2)] = o[m];
     }
@@ -204,10 +199,10 @@ __global__ void __launch_bounds__(kThreads) k_dequant_t(DqtArgs a) {
     for (int j = 0; j < 4; ++j) {
       const uint32_t x0 = (&v[0].x)[j], x1 = (&v[1].x)[j], x2 = (&v[2].x)[j],
                      x3 = (&v[3].x)[j];
-      const uint32_t t0 = prmt_u32(x0, x1, 0x5140u), t1 = prmt_u32(x0, x1, 0x7362u);
-      const uint32_t t2 = prmt_u32(x2, x3, 0x5140u), t3 = prmt_u32(x2, x3, 0x7362u);
-      const uint32_t o[4] = {prmt_u32(t0, t2, 0x5410u), prmt_u32(t0, t2, 0x7632u),
-                             prmt_u32(t1, t3, 0x5410u), prmt_u32(t1, t3, 0x7632u)};
+      const uint32_t t0 = prmt(x0, x1, 0x5140u), t1 = prmt(x0, x1, 0x7362u);
+      const uint32_t t2 = prmt(x2, x3, 0x5140u), t3 = prmt(x2, x3, 0x7362u);
+      const uint32_t o[4] = {prmt(t0, t2, 0x5410u), prmt(t0, t2, 0x7632u),
+                             prmt(t1, t3, 0x5410u), prmt(t1, t3, 0x7632u)};
 #pragma unroll
       for (int m = 0; m < 4; ++m) ctile[16 * lb + 4 * j + m][la ^ (lb << 2)] = o[m];
     }
