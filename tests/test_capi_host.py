@@ -122,6 +122,45 @@ def test_bridge_entry_points_reject_bad_arguments():
     assert L.brc_int4_tiles(p, 16, 128, p, None, 7, p, p, None, None) == _lib.BRC_ERR_DTYPE
 
 
+def test_layout_entry_points_reject_bad_arguments():
+    """breccia-orientation layout entry points (transposing dequantize, byte
+    transpose): every rejection happens on the host, before any CUDA call."""
+    L = _lib.lib()
+    raw, p = _buf(256)
+    F32, BF16, E4M3 = _lib.DTYPE_F32, _lib.DTYPE_BF16, _lib.FP8_E4M3
+    MX, NV, I4, PT = _lib.STE_MXFP8, _lib.STE_NVFP4, _lib.STE_INT4, _lib.KIND_PERTENSOR_FP8
+    S32 = _lib.SCALE_F32
+
+    def dqt(codes=p, rows=8, cols=32, kind=MX, fmt=E4M3, block=32, signed=0, sdt=S32,
+            scales=p, zp=None, out=p, odt=BF16):
+        return L.brc_dequant_transposed(codes, rows, cols, kind, fmt, block, signed, sdt, scales,
+                                        zp, out, odt, None)
+    assert dqt(rows=-8) == _lib.BRC_ERR_SHAPE
+    assert dqt(codes=None) == _lib.BRC_ERR_NULL
+    assert dqt(scales=None) == _lib.BRC_ERR_NULL
+    assert dqt(out=None) == _lib.BRC_ERR_NULL
+    assert dqt(odt=9) == _lib.BRC_ERR_DTYPE
+    assert dqt(fmt=5) == _lib.BRC_ERR_DTYPE
+    assert dqt(kind=7) == _lib.BRC_ERR_UNSUPPORTED
+    assert dqt(rows=12) == _lib.BRC_ERR_SHAPE            # rows % 8
+    assert dqt(cols=48) == _lib.BRC_ERR_SHAPE            # cols % 32 for MXFP8
+    assert dqt(kind=NV, cols=24) == _lib.BRC_ERR_SHAPE   # cols % 16
+    assert dqt(kind=I4, block=40, cols=80) == _lib.BRC_ERR_SHAPE  # block % 16
+    assert dqt(kind=I4, block=32, sdt=7) == _lib.BRC_ERR_DTYPE
+    assert dqt(codes=None, scales=None, out=None, rows=0) == _lib.BRC_OK  # empty: no launch
+    assert dqt(kind=PT, codes=p + 4) == _lib.BRC_ERR_ALIGN
+    assert dqt(out=p + 2, odt=F32) == _lib.BRC_ERR_ALIGN
+
+    assert L.brc_transpose_u8(p, -16, 16, p, None) == _lib.BRC_ERR_SHAPE
+    assert L.brc_transpose_u8(p, 24, 16, p, None) == _lib.BRC_ERR_SHAPE   # rows % 16
+    assert L.brc_transpose_u8(p, 16, 8, p, None) == _lib.BRC_ERR_SHAPE    # cols % 16
+    assert L.brc_transpose_u8(None, 16, 16, p, None) == _lib.BRC_ERR_NULL
+    assert L.brc_transpose_u8(p, 16, 16, None, None) == _lib.BRC_ERR_NULL
+    assert L.brc_transpose_u8(None, 0, 16, None, None) == _lib.BRC_OK
+    assert L.brc_transpose_u8(p + 8, 16, 16, p, None) == _lib.BRC_ERR_ALIGN
+    del raw
+
+
 def test_fused_cast_gemm_rejects_bad_arguments():
     """brc_cast_gemm_pertensor_fp8 / brc_cast_pertensor_fp8_delayed check
     everything on the host before the first CUDA call."""
